@@ -1,0 +1,416 @@
+"""Decode-throughput benchmark of the B200 integer datapath (bit-exact int8).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N
+
+Workload (the data-parallel config quoted at 1/2/4/8 GPUs):
+Qwen2.5-0.5B architecture with random N(0, 0.02) weights and QKV bias, quantized int8
+per-channel; per GPU 128 independent sequences of 512 uniform-random prompt tokens, then
+greedy decode with the reference runtime's launch rule (255 decode launches: the 256th
+token is emitted without a launch because position 767 is the last of max_seq 768).
+One *step* is that whole decode phase for the GPU's 128 sequences, starting from the
+prefilled KV cache; prefill runs once, untimed.  Multi-GPU is data parallel: every rank
+decodes its own 128 sequences with no collective ("weak" scaling); the timing is the max
+over ranks.
+
+Printed on rank 0: one JSON line with value (decode tokens/s over all GPUs, device-resident
+tokens), e2e (the same metric through the C ABI host loop with host token buffers and a
+host argmax read per launch), roofline of the dominant kernel, CPU baseline (the numpy
+oracle port of the reference's golden model on this host), clocks and launch counts.
+
+--impl reference times the reference algorithm's CPU implementation (the oracle port; the
+reference's Python package does not exist on the GPU box) on a bounded sample of the same
+workload, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c3")
+    ap.add_argument("--batch", type=int, default=None, help="sequences per GPU (default: the config's)")
+    ap.add_argument("--prompt", type=int, default=None)
+    ap.add_argument("--decode", type=int, default=None)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--artefacts", default=os.environ.get("LLX_ARTEFACTS", str(Path(tempfile.gettempdir()) / "llx_artefacts")))
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--cpu-decode", type=int, default=8, help="decode launches in the CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemm-path", type=int, default=0)
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------------------
+class Dist:
+    def __init__(self, want: int) -> None:
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+        if want != self.world and self.world > 1:
+            raise SystemExit(f"--gpus {want} but WORLD_SIZE {self.world}")
+
+    def barrier(self) -> None:
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self) -> None:
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int) -> None:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            ids = [v.strip() for v in vis.split(",") if v.strip()]
+            self.device = ids[device] if device < len(ids) else device
+        else:
+            self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax = float(parts[1])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------------------
+def workload(args):
+    from llaccel_b200 import artefacts as A
+    cfg = A.CONFIGS[args.config]
+    w = dict(A.WORKLOADS[args.config])
+    if args.batch:
+        w["batch"] = args.batch
+    if args.prompt:
+        w["prompt"] = args.prompt
+    if args.decode:
+        w["decode"] = args.decode
+    n_dec = min(w["decode"], max(0, cfg.max_seq - w["prompt"] - 1))
+    return cfg, w, n_dec
+
+
+def make_artefact(args, dist: Dist) -> Path:
+    from llaccel_b200 import artefacts as A
+    root = Path(args.artefacts)
+    root.mkdir(parents=True, exist_ok=True)
+    if dist.rank == 0:
+        d = A.ensure_artefact(args.config, root, seed=0, fusion=True, device="cuda")
+    dist.barrier()
+    return root / f"{args.config}_s0_v2"
+
+
+def prompts_for(rank: int, B: int, L: int, vocab: int) -> np.ndarray:
+    return np.random.default_rng(1000 + rank).integers(0, vocab, (B, L)).astype(np.int32)
+
+
+def algorithmic_decode_bytes(m, prof: list[dict]) -> float:
+    return float(sum(p["bytes"] for p in prof))
+
+
+def cpu_baseline(qdir: Path, prompt: np.ndarray, n_dec: int, gpu_hist: np.ndarray | None) -> dict:
+    """Oracle port on this host: prefill one sequence (untimed), then time n_dec decode
+    launches; compare the tokens with the GPU's decode history of the same sequence."""
+    import os as _os
+    from oracle import golden_oracle as O
+    cores = _os.cpu_count() or 1
+    o = O.OracleModel(qdir)
+    toks = [int(t) for t in prompt]
+    rows = o.prefill(toks)
+    nxt = int(np.argmax(rows[-1][: o.vocab]))
+    got = []
+    t0 = time.perf_counter()
+    pos = len(toks)
+    for i in range(n_dec):
+        lg = o.decode(nxt, pos + i)
+        nxt = int(np.argmax(lg[: o.vocab]))
+        got.append(nxt)
+    dt = time.perf_counter() - t0
+    parity = None
+    if gpu_hist is not None:
+        parity = bool(gpu_hist[: n_dec].tolist() == got)
+    return {"value": n_dec / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"1 sequence, {n_dec} decode launches at positions {pos}..{pos + n_dec - 1} after an untimed "
+                      f"{len(toks)}-token prefill (numpy oracle of golden.py, BLAS threads = {cores}); "
+                      f"the reference decodes batch sequences one after another, so this is its tokens/s",
+            "parity_vs_gpu": parity}
+
+
+def run_reference(args, dist: Dist) -> None:
+    """--impl reference: the reference algorithm's CPU implementation, rank 0 only."""
+    cfg, w, n_dec = workload(args)
+    if dist.rank != 0:
+        return
+    from llaccel_b200 import artefacts as A
+    root = Path(args.artefacts)
+    qdir = A.ensure_artefact(args.config, root, seed=0, fusion=True, device="cuda" if _has_cuda() else "cpu")
+    from oracle import golden_oracle as O
+    cores = os.cpu_count() or 1
+    o = O.OracleModel(qdir)
+    prompt = prompts_for(0, 1, w["prompt"], cfg.vocab)[0].tolist()
+    rows = o.prefill(prompt)
+    nxt = int(np.argmax(rows[-1][: o.vocab]))
+    per_step = max(1, min(args.cpu_decode, n_dec))
+    pos0 = len(prompt)
+
+    def step():
+        t = nxt
+        for i in range(per_step):
+            t = int(np.argmax(o.decode(t, pos0 + i)[: o.vocab]))
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    value = per_step * args.steps / dt
+    sample = (f"1 of {w['batch']} sequences, {per_step} decode launches per step at positions "
+              f"{pos0}..{pos0 + per_step - 1} after an untimed {len(prompt)}-token prefill; numpy oracle port of "
+              f"golden.py (the reference package is not installed on the GPU box)")
+    line = {"impl": "reference", "metric": f"decode tokens/s (bit-exact int8), {cfg.name}", "value": value,
+            "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"{cfg.name}: {w['batch']} seq/GPU, prompt {w['prompt']}, {n_dec} decode launches",
+                       "parallelism": f"dp{args.gpus}"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def _has_cuda() -> bool:
+    try:
+        import torch
+        return torch.cuda.is_available()
+    except Exception:
+        return False
+
+
+def run_ours(args, dist: Dist) -> None:
+    import torch
+    from llaccel_b200 import build
+    build.build()
+    from llaccel_b200.cuda_backend import CudaModel
+
+    cfg, w, n_dec = workload(args)
+    dev = dist.local
+    torch.cuda.set_device(dev)
+    qdir = make_artefact(args, dist)
+    B, L = w["batch"], w["prompt"]
+    prompts = prompts_for(dist.rank, B, L, cfg.vocab)
+    m = CudaModel(qdir, batch=B, device=dev, max_rows=min(L, 512), gemm_path=args.gemm_path)
+    t0 = time.perf_counter()
+    recs = m.generate_batch(prompts.tolist(), 0, with_logits=False)  # prefill (untimed)
+    prefill_s = time.perf_counter() - t0
+    first = np.array([r["argmax_per_step"][-1] for r in recs], np.int32)
+    stream = torch.cuda.ExternalStream(m.stream_handle(), device=dev)
+
+    def step():
+        m.set_tokens(first)
+        m.decode_async(L, n_dec)
+
+    for _ in range(args.warmup):
+        step()
+    m.sync()
+    hist = m.history(n_dec)
+    clocks = ClockSampler(dev)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # set_tokens synchronises the session stream; decode launches are asynchronous
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    m.sync()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    clock = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    ms_max = dist.max(ms)
+    total_tokens = dist.world * B * n_dec * args.steps
+    value = total_tokens / (ms_max / 1e3)
+    # the decode history must be identical every step (same prompt state, same tokens)
+    hist2 = m.history(n_dec)
+    deterministic = bool(np.array_equal(hist, hist2))
+
+    # per-kernel profile at the middle decode position (roofline of the dominant kernel)
+    pos_mid = L + n_dec // 2
+    prof = m.profile_decode(pos_mid, iters=20)
+    launches_per_step = m.decode_launches_per_step()
+    step_ms_sum = sum(p["ms"] for p in prof)
+    dom = max(prof, key=lambda p: p["ms"])
+    peaks = {}
+    pk = REPO / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peaks = json.loads(pk.read_text())
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    dom_gbs = dom["bytes"] / (dom["ms"] / 1e3) / 1e9
+    roof = {"bound": "hbm", "kernel": dom["label"], "achieved": dom_gbs, "peak": hbm, "unit": "GB/s",
+            "frac": dom_gbs / hbm, "peak_source": peak_src, "traffic": None,
+            "bytes_per_launch": dom["bytes"], "ms_per_launch": dom["ms"], "share_of_step": dom["ms"] / step_ms_sum}
+    step_bytes = sum(p["bytes"] for p in prof)
+    step_ms_graph = ms_max / args.steps / n_dec
+    whole = {"decode_launch_ms": step_ms_graph, "algorithmic_bytes_per_launch": step_bytes,
+             "achieved_gbs": step_bytes / (step_ms_graph / 1e3) / 1e9,
+             "frac_of_hbm": step_bytes / (step_ms_graph / 1e3) / 1e9 / hbm, "kernels_sum_ms": step_ms_sum}
+
+    # e2e: the C-ABI host loop, host token buffers in, host argmax out, per decode launch
+    e2e_steps = max(1, args.e2e_steps)
+    tok = np.ascontiguousarray(first.reshape(B, 1))
+    am = np.zeros(B, np.int32)
+    import ctypes as C
+    from llaccel_b200.cuda_backend import _check, _p32
+    lib, sess = m.lib, m._sess
+    dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        cur = tok.copy()
+        for i in range(n_dec):
+            _check(lib, lib.llx_run(sess, _p32(cur), 1, L + i, None, 0, None, _p32(am)))
+            cur[:, 0] = am
+    e2e_s = dist.max(time.perf_counter() - t0)
+    e2e_ok = bool(np.array_equal(cur[:, 0], hist[n_dec - 1]))
+    e2e_value = dist.world * B * n_dec * e2e_steps / e2e_s
+    h2d = n_dec * (B * 4 + 8)
+    d2h = n_dec * (B * 4 + 4)
+
+    base = None
+    if dist.rank == 0 and not args.no_cpu_baseline:
+        base = cpu_baseline(qdir, prompts[0], min(args.cpu_decode, n_dec), hist[:, 0])
+    line = {
+        "metric": f"decode tokens/s (bit-exact int8), {cfg.name}",
+        "value": value, "unit": "tokens/s", "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic",
+        "config": {"workload": f"{cfg.name} (Qwen2.5-0.5B arch, QKV bias) decode: {B} seq/GPU, prompt {L}, "
+                               f"{n_dec} decode launches/step",
+                   "global_batch": B * dist.world, "seq_len": L + n_dec, "prompt": L, "decode_launches": n_dec,
+                   "parallelism": f"dp{dist.world}",
+                   "l2": "inputs larger than L2: every decode launch streams ~1 GB of weights + KV",
+                   "prefill_s_untimed": prefill_s},
+        "roofline": roof, "decode_launch": whole,
+        "cpu_baseline": base,
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "steps": e2e_steps, "path": "llx_run per decode launch (C ABI, host buffers)",
+                "tokens_match_device_loop": e2e_ok},
+        "clocks": clock,
+        "gpu_launches": launches_per_step * n_dec * args.steps,
+        "determinism": deterministic,
+        "profile": [{"k": p["label"], "ms": round(p["ms"], 5), "GBs": round(p["bytes"] / max(p["ms"], 1e-9) / 1e6, 1)}
+                    for p in sorted(prof, key=lambda p: -p["ms"])[:12]],
+    }
+    if dist.rank == 0:
+        print(json.dumps(line), flush=True)
+    m.close()
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        # the reference arm is CPU work on rank 0; other ranks exit without work
+        rank = int(os.environ.get("RANK", "0"))
+        if rank == 0:
+            run_reference(args, Dist(1) if int(os.environ.get("WORLD_SIZE", "1")) == 1 else _NoDist())
+        return
+    dist = Dist(args.gpus)
+    try:
+        run_ours(args, dist)
+    finally:
+        dist.close()
+
+
+class _NoDist:
+    rank, world, local = 0, 1, 0
+
+    def barrier(self):
+        pass
+
+
+if __name__ == "__main__":
+    main()

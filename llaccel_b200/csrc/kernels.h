@@ -1,0 +1,88 @@
+// Launch wrappers for the sm_100a kernels of the integer datapath.
+// Every wrapper enqueues on `st` and returns cudaGetLastError() of the launch.
+// Position-dependent kernels read POS from device memory (`d_pos`) so that a captured
+// CUDA graph replays for any position.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace llx {
+
+// ---- vector engine ----------------------------------------------------------------------
+// tokens [R] (< 0 = zero pad row) -> out [R][dim] i16 rows of `embed`
+cudaError_t launch_embed(const int32_t* tokens, const int16_t* embed, int16_t* out, int R, int dim, int vocab_rows,
+                         int32_t* err, cudaStream_t st);
+
+// rows x [nrows][K] -> y [nrows][K]; optional fused quant to y8 (M_q, S_q)
+cudaError_t launch_rmsnorm(const int16_t* x, const int16_t* gamma, int16_t* y, int8_t* y8, int nrows, int K,
+                           int64_t eps_t, int64_t C, int sh_post, int64_t Mq, int Sq, cudaStream_t st);
+
+cudaError_t launch_quant(const int16_t* x, int8_t* y, int64_t n, int64_t M, int S, cudaStream_t st);
+
+// RoPE over x [R][H*D] (row r at position pos + r % M); y16 gets the rotated i16 rows;
+// optional fused quant into y8; with kcache also writes y8 rows into
+// kcache[b][h][pos + m][:] (b = r / M, cache [B][H][max_seq][D]).
+cudaError_t launch_rope(const int16_t* x, int16_t* y16, int8_t* y8, int64_t Mq, int Sq, int8_t* kcache, int R, int M,
+                        int H, int D, const int16_t* cos_tab, const int16_t* sin_tab, const int* d_pos, int max_seq,
+                        cudaStream_t st);
+
+// k, v [R][Hkv*D] i8 -> caches [B][Hkv][max_seq][D] at positions pos + m
+cudaError_t launch_kv_write(const int8_t* k, const int8_t* v, int8_t* kc, int8_t* vc, int R, int M, int Hkv, int D,
+                            const int* d_pos, int max_seq, cudaStream_t st);
+
+cudaError_t launch_add(const int16_t* a, const int16_t* b, int16_t* y, int64_t n, int sh_b, cudaStream_t st);
+cudaError_t launch_mul(const int16_t* a, const int16_t* b, int16_t* y, int64_t n, int sh, cudaStream_t st);
+// luts: device tables laid out as numerics.cuh kLut* (sigmoid, exp-int, exp-frac)
+cudaError_t launch_silu(const int16_t* x, int16_t* y, int64_t n, int64_t Mi, int Si, int sh_out,
+                        const uint16_t* luts, cudaStream_t st);
+
+// logits [R][ld] i16 -> argmax over the first `vocab` entries (lowest index on ties)
+cudaError_t launch_argmax(const int16_t* logits, int R, int ld, int vocab, int32_t* out, cudaStream_t st);
+
+// dst[i][:] = src[idx[i]][:] for i < n (row bytes multiple of 16)
+cudaError_t launch_gather_rows(const void* src, void* dst, const int32_t* idx, int n, int row_bytes,
+                               cudaStream_t st);
+
+// ---- matrix engine ------------------------------------------------------------------------
+enum Epilogue : int { EPI_NONE = 0, EPI_RESADD = 1, EPI_SILU = 2, EPI_MUL = 3 };
+
+struct LinearArgs {
+  const int8_t* A;      // [R][K] i8, row stride K
+  const int8_t* W;      // [N][K] i8 row-major
+  const int32_t* bias;  // [N] or null
+  const int32_t* rq;    // [N][2] {M, S}
+  const int16_t* aux;   // [R][N] i16 (RESADD / MUL) or null
+  void* out;            // [R][N] i16, or i8 when out_i8
+  int R, N, K;
+  int out_i8;
+  int epi;
+  int64_t silu_Mi;
+  int silu_Si, silu_sh;
+  int aux_shift;
+  const uint16_t* luts;  // device tables (SILU epilogue)
+};
+
+// CUDA-core paths: 0 = auto, 1 = GEMV (small R), 2 = tiled dp4a
+cudaError_t launch_linear(const LinearArgs& a, int path, cudaStream_t st);
+
+// ---- attention engine -------------------------------------------------------------------
+struct AttnArgs {
+  const int8_t* q;   // [R][H*D]
+  const int8_t* kc;  // [B][Hkv][max_seq][D]
+  const int8_t* vc;
+  int8_t* out;       // [R][H*D]
+  int B, M, H, Hkv, D, max_seq;
+  const int* d_pos;
+  int pos_hint;      // host copy of pos (sizes shared memory; must be >= the device value)
+  int64_t Ms, Mo;
+  int Ss, So;
+  int prob_bits;
+  const uint16_t* luts;  // device tables (exp LUTs)
+};
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st);
+// opt the attention kernel into `smem` bytes of dynamic shared memory (once per device, before capture)
+cudaError_t prepare_attention(size_t smem);
+size_t attention_smem_bytes(int H, int Hkv, int D, int T);
+
+}  // namespace llx

@@ -1,0 +1,317 @@
+// Vector-engine kernels: embedding gather, RMSNorm(+QUANT), QUANT, RoPE(+QUANT+K write),
+// KV write, ADD, MUL, SILU, argmax, row gather.  One warp per row for the row
+// reductions; 16-byte loads and stores everywhere the row width allows (every width on
+// this path is a multiple of 16 elements, NUMERICS.md "Counts are multiples of 16").
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kernels.h"
+#include "numerics.cuh"
+
+namespace llx {
+
+
+static inline unsigned grid1d(int64_t n, int per_block) { return (unsigned)((n + per_block - 1) / per_block); }
+
+// ---- embedding gather (golden.py:369-373; host.cpp:108-113) ------------------------------
+__global__ void k_embed(const int32_t* __restrict__ tokens, const int16_t* __restrict__ embed,
+                        int16_t* __restrict__ out, int R, int dim, int vocab_rows, int32_t* err) {
+  const int r = blockIdx.x;
+  const int tok = tokens[r];
+  const int chunks = dim / 8;
+  uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)r * dim);
+  if (tok < 0 || tok >= vocab_rows) {
+    if (tok >= vocab_rows && threadIdx.x == 0 && err) atomicExch(err, 1);
+    for (int c = threadIdx.x; c < chunks; c += blockDim.x) dst[c] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(embed + (int64_t)tok * dim);
+  for (int c = threadIdx.x; c < chunks; c += blockDim.x) dst[c] = src[c];
+}
+
+cudaError_t launch_embed(const int32_t* tokens, const int16_t* embed, int16_t* out, int R, int dim, int vocab_rows,
+                         int32_t* err, cudaStream_t st) {
+  if (R <= 0) return cudaSuccess;
+  k_embed<<<R, 64, 0, st>>>(tokens, embed, out, R, dim, vocab_rows, err);
+  return cudaGetLastError();
+}
+
+// ---- RMSNorm (numerics.h:60-71; NUMERICS.md:88-111), optionally fused with QUANT -----------
+__device__ __forceinline__ void unpack8(const uint4& v, int32_t* o) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    o[2 * i] = (int16_t)(w[i] & 0xFFFF);
+    o[2 * i + 1] = (int16_t)(w[i] >> 16);
+  }
+}
+__device__ __forceinline__ uint4 pack8(const int32_t* v) {
+  uint4 r;
+  r.x = (uint32_t)(uint16_t)v[0] | ((uint32_t)(uint16_t)v[1] << 16);
+  r.y = (uint32_t)(uint16_t)v[2] | ((uint32_t)(uint16_t)v[3] << 16);
+  r.z = (uint32_t)(uint16_t)v[4] | ((uint32_t)(uint16_t)v[5] << 16);
+  r.w = (uint32_t)(uint16_t)v[6] | ((uint32_t)(uint16_t)v[7] << 16);
+  return r;
+}
+__device__ __forceinline__ uint2 pack8_i8(const int32_t* v) {
+  uint2 r;
+  r.x = (uint32_t)(uint8_t)v[0] | ((uint32_t)(uint8_t)v[1] << 8) | ((uint32_t)(uint8_t)v[2] << 16) |
+        ((uint32_t)(uint8_t)v[3] << 24);
+  r.y = (uint32_t)(uint8_t)v[4] | ((uint32_t)(uint8_t)v[5] << 8) | ((uint32_t)(uint8_t)v[6] << 16) |
+        ((uint32_t)(uint8_t)v[7] << 24);
+  return r;
+}
+
+__global__ void k_rmsnorm(const int16_t* __restrict__ x, const int16_t* __restrict__ gamma, int16_t* __restrict__ y,
+                          int8_t* __restrict__ y8, int nrows, int K, int64_t eps_t, int64_t C, int sh_post,
+                          int64_t Mq, int Sq) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= nrows) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)warp * K);
+  const uint4* gr = reinterpret_cast<const uint4*>(gamma);
+  const int chunks = K / 8;
+  uint64_t ss = 0;
+  for (int c = lane; c < chunks; c += 32) {
+    int32_t v[8];
+    unpack8(xr[c], v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += (uint64_t)((int64_t)v[i] * v[i]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  // every lane holds the full sum; the serial isqrt/udiv is cheap enough to replicate
+  const uint64_t tt = ss + (uint64_t)eps_t;
+  const uint32_t r = isqrt48(tt);
+  uint64_t inv = udiv((uint64_t)C, r > 1 ? r : 1);
+  if (inv > 65535) inv = 65535;
+  uint4* yr = reinterpret_cast<uint4*>(y + (int64_t)warp * K);
+  uint2* yq = y8 ? reinterpret_cast<uint2*>(y8 + (int64_t)warp * K) : nullptr;
+  for (int c = lane; c < chunks; c += 32) {
+    int32_t v[8], g[8], o[8];
+    unpack8(xr[c], v);
+    unpack8(gr[c], g);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t xg = (int64_t)v[i] * g[i];
+      o[i] = (int32_t)sat16(rshr(xg * (int64_t)inv, sh_post));
+    }
+    yr[c] = pack8(o);
+    if (yq) {
+      int32_t q[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) q[i] = (int32_t)sat8(mulshift(o[i], Mq, Sq));
+      yq[c] = pack8_i8(q);
+    }
+  }
+}
+
+cudaError_t launch_rmsnorm(const int16_t* x, const int16_t* gamma, int16_t* y, int8_t* y8, int nrows, int K,
+                           int64_t eps_t, int64_t C, int sh_post, int64_t Mq, int Sq, cudaStream_t st) {
+  if (nrows <= 0) return cudaSuccess;
+  const int warps_per_block = 4;
+  k_rmsnorm<<<grid1d(nrows, warps_per_block), 32 * warps_per_block, 0, st>>>(x, gamma, y, y8, nrows, K, eps_t, C,
+                                                                             sh_post, Mq, Sq);
+  return cudaGetLastError();
+}
+
+// ---- QUANT i16 -> i8 (numerics.h:56) -------------------------------------------------------
+__global__ void k_quant(const int16_t* __restrict__ x, int8_t* __restrict__ y, int64_t n8, int64_t M, int S) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  int32_t v[8], q[8];
+  unpack8(reinterpret_cast<const uint4*>(x)[i], v);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) q[k] = (int32_t)sat8(mulshift(v[k], M, S));
+  reinterpret_cast<uint2*>(y)[i] = pack8_i8(q);
+}
+
+cudaError_t launch_quant(const int16_t* x, int8_t* y, int64_t n, int64_t M, int S, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  const int64_t n8 = n / 8;
+  k_quant<<<grid1d(n8, 256), 256, 0, st>>>(x, y, n8, M, S);
+  return cudaGetLastError();
+}
+
+// ---- RoPE (numerics.h:75-84; NUMERICS.md:113-125) [+ QUANT] [+ K cache write] ------------
+// thread per (row, head, i < D/2): rotates the (i, i + D/2) pair.
+__global__ void k_rope(const int16_t* __restrict__ x, int16_t* __restrict__ y16, int8_t* __restrict__ y8,
+                       int64_t Mq, int Sq, int8_t* __restrict__ kcache, int R, int M, int H, int D,
+                       const int16_t* __restrict__ cos_tab, const int16_t* __restrict__ sin_tab,
+                       const int* __restrict__ d_pos, int max_seq) {
+  const int half = D >> 1;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = (int64_t)R * H * half;
+  if (idx >= total) return;
+  const int i = (int)(idx % half);
+  const int h = (int)((idx / half) % H);
+  const int r = (int)(idx / ((int64_t)half * H));
+  const int m = r % M;
+  const int p = *d_pos + m;
+  const int64_t base = (int64_t)r * H * D + (int64_t)h * D;
+  const int64_t x1 = x[base + i], x2 = x[base + i + half];
+  const int64_t c = cos_tab[(int64_t)p * half + i], s = sin_tab[(int64_t)p * half + i];
+  const int64_t a = sat16(rshr(x1 * c - x2 * s, 14));
+  const int64_t b = sat16(rshr(x2 * c + x1 * s, 14));
+  y16[base + i] = (int16_t)a;
+  y16[base + i + half] = (int16_t)b;
+  if (y8) {
+    const int8_t qa = (int8_t)sat8(mulshift(a, Mq, Sq)), qb = (int8_t)sat8(mulshift(b, Mq, Sq));
+    y8[base + i] = qa;
+    y8[base + i + half] = qb;
+    if (kcache) {
+      const int bseq = r / M;
+      int8_t* dst = kcache + (((int64_t)bseq * H + h) * max_seq + p) * D;
+      dst[i] = qa;
+      dst[i + half] = qb;
+    }
+  }
+}
+
+cudaError_t launch_rope(const int16_t* x, int16_t* y16, int8_t* y8, int64_t Mq, int Sq, int8_t* kcache, int R, int M,
+                        int H, int D, const int16_t* cos_tab, const int16_t* sin_tab, const int* d_pos, int max_seq,
+                        cudaStream_t st) {
+  const int64_t total = (int64_t)R * H * (D / 2);
+  if (total <= 0) return cudaSuccess;
+  k_rope<<<grid1d(total, 256), 256, 0, st>>>(x, y16, y8, Mq, Sq, kcache, R, M, H, D, cos_tab, sin_tab, d_pos,
+                                             max_seq);
+  return cudaGetLastError();
+}
+
+// ---- KV write (golden.py:344-351; funcsim.cpp:377-396) ----------------------------------
+// thread per 16-byte chunk of one (row, kv head) segment
+__global__ void k_kv_write(const int8_t* __restrict__ k, const int8_t* __restrict__ v, int8_t* __restrict__ kc,
+                           int8_t* __restrict__ vc, int R, int M, int Hkv, int D, const int* __restrict__ d_pos,
+                           int max_seq) {
+  const int cpr = D / 16;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = (int64_t)R * Hkv * cpr;
+  if (idx >= total) return;
+  const int c = (int)(idx % cpr);
+  const int h = (int)((idx / cpr) % Hkv);
+  const int r = (int)(idx / ((int64_t)cpr * Hkv));
+  const int bseq = r / M, m = r % M;
+  const int p = *d_pos + m;
+  const int64_t src = (int64_t)r * Hkv * D + (int64_t)h * D + c * 16;
+  const int64_t dst = (((int64_t)bseq * Hkv + h) * max_seq + p) * D + c * 16;
+  if (k) *reinterpret_cast<uint4*>(kc + dst) = *reinterpret_cast<const uint4*>(k + src);
+  if (v) *reinterpret_cast<uint4*>(vc + dst) = *reinterpret_cast<const uint4*>(v + src);
+}
+
+cudaError_t launch_kv_write(const int8_t* k, const int8_t* v, int8_t* kc, int8_t* vc, int R, int M, int Hkv, int D,
+                            const int* d_pos, int max_seq, cudaStream_t st) {
+  const int64_t total = (int64_t)R * Hkv * (D / 16);
+  if (total <= 0) return cudaSuccess;
+  k_kv_write<<<grid1d(total, 256), 256, 0, st>>>(k, v, kc, vc, R, M, Hkv, D, d_pos, max_seq);
+  return cudaGetLastError();
+}
+
+// ---- elementwise ADD / MUL / SILU (numerics.h:45-55) ----------------------------------------
+__global__ void k_add(const int16_t* __restrict__ a, const int16_t* __restrict__ b, int16_t* __restrict__ y,
+                      int64_t n8, int sh_b) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  int32_t va[8], vb[8], o[8];
+  unpack8(reinterpret_cast<const uint4*>(a)[i], va);
+  unpack8(reinterpret_cast<const uint4*>(b)[i], vb);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) o[k] = (int32_t)sat16((int64_t)va[k] + rshr(vb[k], sh_b));
+  reinterpret_cast<uint4*>(y)[i] = pack8(o);
+}
+
+__global__ void k_mul(const int16_t* __restrict__ a, const int16_t* __restrict__ b, int16_t* __restrict__ y,
+                      int64_t n8, int sh) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  int32_t va[8], vb[8], o[8];
+  unpack8(reinterpret_cast<const uint4*>(a)[i], va);
+  unpack8(reinterpret_cast<const uint4*>(b)[i], vb);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) o[k] = (int32_t)sat16(rshr((int64_t)va[k] * vb[k], sh));
+  reinterpret_cast<uint4*>(y)[i] = pack8(o);
+}
+
+__global__ void k_silu(const int16_t* __restrict__ x, int16_t* __restrict__ y, int64_t n8, int64_t Mi, int Si,
+                       int sh_out, const uint16_t* __restrict__ sig) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  int32_t v[8], o[8];
+  unpack8(reinterpret_cast<const uint4*>(x)[i], v);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) o[k] = (int32_t)silu16(v[k], Mi, Si, sh_out, sig);
+  reinterpret_cast<uint4*>(y)[i] = pack8(o);
+}
+
+cudaError_t launch_add(const int16_t* a, const int16_t* b, int16_t* y, int64_t n, int sh_b, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_add<<<grid1d(n / 8, 256), 256, 0, st>>>(a, b, y, n / 8, sh_b);
+  return cudaGetLastError();
+}
+cudaError_t launch_mul(const int16_t* a, const int16_t* b, int16_t* y, int64_t n, int sh, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_mul<<<grid1d(n / 8, 256), 256, 0, st>>>(a, b, y, n / 8, sh);
+  return cudaGetLastError();
+}
+cudaError_t launch_silu(const int16_t* x, int16_t* y, int64_t n, int64_t Mi, int Si, int sh_out,
+                        const uint16_t* luts, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_silu<<<grid1d(n / 8, 256), 256, 0, st>>>(x, y, n / 8, Mi, Si, sh_out, luts + kLutSig);
+  return cudaGetLastError();
+}
+
+// ---- argmax over the first `vocab` logits, lowest index on ties (NUMERICS.md:207-208) --------
+__global__ void k_argmax(const int16_t* __restrict__ logits, int ld, int vocab, int32_t* __restrict__ out) {
+  const int r = blockIdx.x;
+  const int16_t* row = logits + (int64_t)r * ld;
+  // key: value in the high half, inverted index in the low half -> max key = first max
+  unsigned long long best = 0;
+  for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+    const unsigned long long key =
+        ((unsigned long long)(uint32_t)((int32_t)row[i] + 32768) << 32) | (0xFFFFFFFFu - (uint32_t)i);
+    best = key > best ? key : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  __shared__ unsigned long long warp_best[32];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) warp_best[w] = best;
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x >> 5;
+    best = lane < nw ? warp_best[lane] : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
+    if (lane == 0) out[r] = (int32_t)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
+  }
+}
+
+cudaError_t launch_argmax(const int16_t* logits, int R, int ld, int vocab, int32_t* out, cudaStream_t st) {
+  if (R <= 0) return cudaSuccess;
+  k_argmax<<<R, 512, 0, st>>>(logits, ld, vocab, out);
+  return cudaGetLastError();
+}
+
+// ---- row gather ----------------------------------------------------------------------------
+__global__ void k_gather_rows(const uint4* __restrict__ src, uint4* __restrict__ dst, const int32_t* __restrict__ idx,
+                              int chunks) {
+  const int i = blockIdx.x;
+  const int64_t s = (int64_t)idx[i] * chunks, d = (int64_t)i * chunks;
+  for (int c = threadIdx.x; c < chunks; c += blockDim.x) dst[d + c] = src[s + c];
+}
+
+cudaError_t launch_gather_rows(const void* src, void* dst, const int32_t* idx, int n, int row_bytes,
+                               cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_gather_rows<<<n, 128, 0, st>>>(reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), idx,
+                                   row_bytes / 16);
+  return cudaGetLastError();
+}
+
+}  // namespace llx

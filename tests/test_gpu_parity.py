@@ -1,0 +1,163 @@
+"""GPU parity: the CUDA backend (through the C ABI) against the reference's golden records
+and against the CPU oracle, bit for bit.  Every comparison here is exact equality: the
+datapath is integer-only, so there is no tolerance."""
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, QGRAPH_FIXTURES
+from oracle import golden_oracle as O
+import qgraph_synth
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("no CUDA device", allow_module_level=True)
+
+from llaccel_b200 import build as _build  # noqa: E402
+
+_build.build()
+from llaccel_b200.cuda_backend import CudaModel  # noqa: E402
+
+
+def _rec(name):
+    rec = json.loads((GOLDEN / name / "golden.json").read_text())
+    return rec, rec["prompt_tokens"], len(rec["generated"])
+
+
+@pytest.mark.parametrize("name", QGRAPH_FIXTURES)
+def test_generate_matches_reference_record(name):
+    rec, prompt, n = _rec(name)
+    with CudaModel(GOLDEN / name) as m:
+        assert m.generate(prompt, n) == rec
+
+
+@pytest.mark.parametrize("name", QGRAPH_FIXTURES)
+def test_host_loop_activations_match_reference(name):
+    rec, prompt, n = _rec(name)
+    want = np.load(GOLDEN / name / "acts.npz")
+    acts: list = []
+    with CudaModel(GOLDEN / name, keep_acts=True, max_rows=16) as m:
+        got = m.generate(prompt, n, acts)
+    assert got == rec
+    for key in want.files:
+        i, kind, pos, act = key.split("|", 3)
+        st = acts[int(i)]
+        assert st["kind"] == kind and st["pos"] == int(pos)
+        np.testing.assert_array_equal(st["acts"][act].astype(np.int32), want[key], err_msg=key)
+
+
+@pytest.mark.parametrize("name", ["fx_v1", "c1_v2", "qwen3_tiny", "d128_tiny"])
+@pytest.mark.parametrize("fuse,gemm_path", [(False, 1), (False, 2), (True, 1), (True, 2)])
+def test_plan_and_gemm_variants_are_identical(name, fuse, gemm_path):
+    rec, prompt, n = _rec(name)
+    with CudaModel(GOLDEN / name, fuse=fuse, gemm_path=gemm_path) as m:
+        assert m.generate(prompt, n) == rec
+        assert m.generate(prompt, n, fast=False) == rec
+
+
+@pytest.mark.parametrize("name", ["c1_v2", "qwen2_tiny", "d128_tiny"])
+def test_batch_matches_oracle_per_sequence(name):
+    o = O.OracleModel(GOLDEN / name)
+    rng = np.random.default_rng(7)
+    B, L, n = 5, 21, 9
+    prompts = rng.integers(0, o.vocab, (B, L)).tolist()
+    with CudaModel(GOLDEN / name, batch=B) as m:
+        for prefill_rows in (None, 0, 16):
+            recs = m.generate_batch(prompts, n, prefill_rows=prefill_rows)
+            for b in range(B):
+                assert recs[b] == o.generate(prompts[b], n), (prefill_rows, b)
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(seed=1),
+    dict(seed=2, fuse=False),
+    dict(seed=3, extreme=True),
+    dict(seed=4, extreme=True, fuse=False, prob_bits=8),
+    dict(seed=5, D=128, H=2, Hkv=1, dim=128, ffn=64, qk_norm=True),
+    dict(seed=6, D=16, H=6, Hkv=3, dim=48, ffn=32, vocab=17, bias=False),
+    dict(seed=7, D=64, H=4, Hkv=4, prefill_m=4, max_seq=48),
+])
+def test_stress_graphs_run_chunk_matches_oracle(tmp_path, cfg):
+    d = qgraph_synth.build(tmp_path / "g", **cfg)
+    o = O.OracleModel(d)
+    rng = np.random.default_rng(cfg["seed"])
+    with CudaModel(d, max_rows=16, keep_acts=True) as m:
+        pos = 0
+        for M in (16, 5, 1, 1, 9, 1):
+            rows = o.embed[rng.integers(0, o.vocab, M)].astype(np.int64)
+            rows[rng.random(M) < 0.2] = 0  # zero pad rows
+            want_acts, got_acts = {}, {}
+            want = o.run_chunk(rows, pos, want_acts)
+            got = m.run_chunk(rows, pos, got_acts)
+            np.testing.assert_array_equal(got, want)
+            for k, v in want_acts.items():
+                np.testing.assert_array_equal(got_acts[k], v, err_msg=f"{k} pos={pos} M={M}")
+            pos += M
+
+
+def test_chunked_prefill_equals_sequential_and_pad_rows(tmp_path):
+    d = GOLDEN / "fx_v1"
+    toks = [(3 + i) % 16 for i in range(21)]
+    with CudaModel(d) as a, CudaModel(d) as b:
+        pa = a.prefill(toks)
+        pb = [b.decode(t, i) for i, t in enumerate(toks)]
+        for x, y in zip(pa, pb):
+            np.testing.assert_array_equal(x, y)
+        a.reset()
+        short = a.prefill(toks[:12])
+        for x, y in zip(pa[:12], short):
+            np.testing.assert_array_equal(x, y)
+
+
+def test_device_decode_loop_matches_records():
+    rec, prompt, n = _rec("c1_v2")
+    B = 3
+    with CudaModel(GOLDEN / "c1_v2", batch=B) as m:
+        recs = m.generate_batch([prompt] * B, 1)
+        # continue with the device-resident loop from the first generated token
+        m.set_tokens([recs[0]["generated"][0]] * B)
+        steps = n - 1
+        m.decode_async(len(prompt), steps)
+        m.sync()
+        h = m.history(steps)
+        for b in range(B):
+            assert h[:, b].tolist() == rec["argmax_per_step"][2 : 2 + steps]
+
+
+def test_errors_mirror_reference():
+    with CudaModel(GOLDEN / "fx_v1") as m:
+        with pytest.raises(ValueError, match="max_seq"):
+            m.generate(list(range(10)), 64)
+        with pytest.raises(ValueError, match="empty prompt"):
+            m.generate([], 3)
+        with pytest.raises(ValueError, match="vocabulary"):
+            m.generate([0, 99], 3)
+        with pytest.raises(ValueError, match="max_seq"):
+            m.run_chunk(np.zeros((16, m.dim)), 60)
+        # the session stays usable after an error
+        rec, prompt, n = _rec("fx_v1")
+        assert m.generate(prompt, n) == rec
+
+
+def test_invalid_qgraphs_are_rejected(tmp_path):
+    import shutil
+    src = GOLDEN / "fx_v1"
+    for mutate, match in [
+        (lambda g: g["ops"][0].__setitem__("sh_post", 64), "shift"),
+        (lambda g: g["ops"][1].__setitem__("S", -1), "shift"),
+        (lambda g: g["model"].__setitem__("prefill_m", 3), "prefill_m"),
+        (lambda g: g["ops"].insert(0, {"op": "conv", "out": "x"}), "unknown qgraph op"),
+        (lambda g: g["ops"][2].__setitem__("N", 31), "N"),
+    ]:
+        d = tmp_path / f"bad{len(list(tmp_path.iterdir()))}"
+        shutil.copytree(src, d)
+        g = json.loads((d / "qgraph.json").read_text())
+        mutate(g)
+        (d / "qgraph.json").write_text(json.dumps(g))
+        with pytest.raises(ValueError, match=match):
+            CudaModel(d)
