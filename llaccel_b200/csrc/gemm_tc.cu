@@ -1,0 +1,460 @@
+// Matrix engine on the 5th-generation tensor cores: tcgen05.mma kind::i8 with TMEM
+// accumulators fed by TMA, and the fused requant epilogue of NUMERICS.md:62-86.
+//
+// CTA tile: 128 activation rows (MMA M) x NT weight channels (MMA N), K streamed in
+// 128-byte blocks through an S-stage shared-memory ring:
+//   warp 0  one thread issues the TMA loads of the activation tile [128 x 128 B] and the
+//           weight tile [NT x 128 B] (both K-major, 128-byte swizzle) into stage s;
+//   warp 1  allocates NT TMEM columns, one thread issues 4 MMAs (K = 32 each) per block
+//           and commits each stage back to the producer, then the accumulator;
+//   warps 2-5 read the int32 accumulator rows from TMEM (one row per thread), add the
+//           bias, requantize per channel, apply the epilogue and store 16 channels at a
+//           time (i16 or i8), row-major.
+// The int32 accumulation is exact (|acc| <= K * 2^14 < 2^31 for K < 2^17), so the tensor
+// core result equals the reference's int64 matmul.  Rows and K past the tensor extents
+// are zero-filled by TMA.  Every mbarrier wait is bounded: on timeout the CTA records an
+// error word, stops issuing work, drains the copies it started and frees its TMEM.
+//
+// Split-K: with ksplit > 1, the CTAs of a thread-block cluster (cluster dims 1 x ksplit)
+// take disjoint K ranges; each writes its accumulator tile to its own shared memory and
+// the cluster's rank-0 CTA sums the partials over DSMEM before the epilogue (integer
+// addition: exact in any order).  No TMA multicast is used anywhere.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kernels.h"
+#include "numerics.cuh"
+
+namespace llx {
+
+namespace tc {
+
+constexpr int BM = 128;         // MMA M: activation rows per tile
+constexpr int BK = 128;         // bytes of K per stage (= the 128-byte swizzle span)
+constexpr int kThreads = 192;   // 6 warps
+constexpr uint32_t kSpinLimit = 1u << 26;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait: false on timeout
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023) == 1023 && *abort) return false;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart
+__device__ __forceinline__ uint64_t smem_desc(const void* p) {
+  const uint64_t addr = smem_u32(p);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;         // start address
+  d |= (uint64_t)1 << 16;               // leading byte offset (16 B, unused with swizzle)
+  d |= (uint64_t)(1024 >> 4) << 32;     // stride byte offset
+  d |= (uint64_t)1 << 46;               // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;               // SWIZZLE_128B
+  return d;
+}
+
+// instruction descriptor: kind::i8, D = s32, A = B = s8, both K-major, M = 128, N = nt
+__host__ __device__ constexpr uint32_t idesc_i8(int nt) {
+  return (2u << 4)                 // D format s32
+         | (1u << 7)               // A signed 8-bit
+         | (1u << 10)              // B signed 8-bit
+         | ((uint32_t)(nt >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* v) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+      "[%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t dsmem_ld(const void* local, uint32_t rank) {
+  uint32_t remote, v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ int64_t epi_value(int32_t acc, int64_t bias, int64_t M, int S, int64_t aux,
+                                             const LinearArgs& a) {
+  const int64_t v = (int64_t)acc + bias;
+  if (a.out_i8) return sat8(mulshift(v, M, S));
+  const int64_t t = sat16(mulshift(v, M, S));
+  switch (a.epi) {
+    case EPI_RESADD: return sat16(t + aux);
+    case EPI_SILU: return silu16(t, a.silu_Mi, a.silu_Si, a.silu_sh, a.luts + kLutSig);
+    case EPI_MUL: return sat16(rshr(t * aux, a.aux_shift));
+    default: return t;
+  }
+}
+
+template <int NT, int S>
+struct Smem {
+  static constexpr int kA = BM * BK;  // 16 KB activation tile
+  static constexpr int kB = NT * BK;  // weight tile
+  static constexpr int kStage = kA + kB;
+  static constexpr int kRing = S * kStage;
+  // partial accumulators for split-K reduction reuse the ring: BM x NT int32
+  static constexpr int kPart = BM * NT * 4;
+  static constexpr int kBytes = (kRing > kPart ? kRing : kPart) + 1024 /* alignment slack */ + 256;
+};
+
+template <int NT, int S>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_linear_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w, LinearArgs a,
+                int ksplit, int32_t* err) {
+  using L = Smem<NT, S>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full_bar[S], empty_bar[S], acc_bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ volatile int abort_flag;
+  __shared__ int issued;  // TMA stages issued by the producer
+  __shared__ int64_t s_M[NT], s_bias[NT];
+  __shared__ int s_S[NT];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * NT;
+  const int m0 = (blockIdx.y / ksplit) * BM;
+  const uint32_t crank = ksplit > 1 ? cluster_rank() : 0;
+  // this CTA's K range in 128-byte blocks
+  const int nkb_total = (a.K + BK - 1) / BK;
+  const int per = (nkb_total + ksplit - 1) / ksplit;
+  const int kb0 = (int)crank * per;
+  const int kb1 = min(nkb_total, kb0 + per);
+  const int nkb = kb1 > kb0 ? kb1 - kb0 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&acc_bar, 1);
+    abort_flag = 0;
+    issued = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"(NT < 32 ? 32 : NT));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  // per-channel requant parameters
+  for (int i = threadIdx.x; i < NT; i += blockDim.x) {
+    const int n = n0 + i;
+    s_M[i] = n < a.N ? (int64_t)a.rq[2 * n] : 0;
+    s_S[i] = n < a.N ? a.rq[2 * n + 1] : 0;
+    s_bias[i] = (n < a.N && a.bias) ? (int64_t)a.bias[n] : 0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer ----
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % S;
+        if (!mbar_wait(&empty_bar[s], ((i / S) + 1) & 1, &abort_flag)) {
+          abort_flag = 1;
+          atomicExch(err, 2);
+          break;
+        }
+        uint8_t* sa = ring + s * L::kStage;
+        uint8_t* sb = sa + L::kA;
+        mbar_expect_tx(&full_bar[s], L::kA + L::kB);
+        const int kx = (kb0 + i) * BK;
+        tma_load_2d(sa, &map_a, &full_bar[s], kx, m0);
+        tma_load_2d(sb, &map_w, &full_bar[s], kx, n0);
+        issued = i + 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer ----
+      const uint32_t idesc = idesc_i8(NT);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % S;
+        if (!mbar_wait(&full_bar[s], (i / S) & 1, &abort_flag)) {
+          abort_flag = 1;
+          atomicExch(err, 3);
+          break;
+        }
+        tc_fence_after();
+        const uint8_t* sa = ring + s * L::kStage;
+        const uint8_t* sb = sa + L::kA;
+        const uint64_t da = smem_desc(sa), db = smem_desc(sb);
+#pragma unroll
+        for (int k = 0; k < BK / 32; ++k) {
+          // advance both descriptors by 32 bytes of K inside the swizzle atom
+          mma_i8(tmem, da + (uint64_t)(k * 2), db + (uint64_t)(k * 2), idesc, (i > 0 || k > 0) ? 1u : 0u);
+        }
+        mma_commit(&empty_bar[s]);
+      }
+      mma_commit(&acc_bar);  // fires once every MMA issued above has completed (or at once if none)
+    }
+  } else {
+    // ---- epilogue warps 2..5: TMEM lane quarter = warp % 4 ----
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    const bool ok = mbar_wait(&acc_bar, 0, &abort_flag);
+    if (!ok) {
+      abort_flag = 1;
+      atomicExch(err, 4);
+    }
+    tc_fence_after();
+    int32_t* part = reinterpret_cast<int32_t*>(ring);  // [BM][NT] partials when ksplit > 1
+    if (ok && ksplit > 1) {
+      // all MMAs are complete, so the ring is free: stage this CTA's partial tile
+#pragma unroll
+      for (int c0 = 0; c0 < NT; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + c0, v);
+        if (nkb == 0) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = 0;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) part[row_in_tile * NT + c0 + j] = (int32_t)v[j];
+      }
+    }
+  }
+  if (ksplit > 1) {
+    // all threads of every CTA in the cluster meet here (partials visible cluster-wide)
+    cluster_sync();
+  }
+  if (warp >= 2 && !abort_flag && (ksplit == 1 || crank == 0)) {
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    const int r = m0 + row_in_tile;
+    int32_t* part = reinterpret_cast<int32_t*>(ring);
+#pragma unroll 1
+    for (int c0 = 0; c0 < NT; c0 += 16) {
+      int32_t acc[16];
+      if (ksplit == 1) {
+        uint32_t v[16];
+        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + c0, v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = nkb > 0 ? (int32_t)v[j] : 0;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = part[row_in_tile * NT + c0 + j];
+        for (uint32_t p = 1; p < (uint32_t)ksplit; ++p)
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[j] += (int32_t)dsmem_ld(part + row_in_tile * NT + c0 + j, p);
+      }
+      if (r >= a.R) continue;
+      const int nb = n0 + c0;
+      if (nb >= a.N) continue;  // N is a multiple of 8; tiles of 16 may straddle only at 8
+      const int cnt = min(16, a.N - nb);
+      int64_t aux[16];
+      if (a.epi == EPI_RESADD || a.epi == EPI_MUL) {
+        const int16_t* ap = a.aux + (int64_t)r * a.N + nb;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) aux[j] = j < cnt ? ap[j] : 0;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) aux[j] = 0;
+      }
+      int32_t o[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[j] = (int32_t)epi_value(acc[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], aux[j], a);
+      if (a.out_i8) {
+        int8_t* op = reinterpret_cast<int8_t*>(a.out) + (int64_t)r * a.N + nb;
+        if (cnt == 16) {
+          uint4 w;
+          w.x = (uint32_t)(uint8_t)o[0] | (uint32_t)(uint8_t)o[1] << 8 | (uint32_t)(uint8_t)o[2] << 16 |
+                (uint32_t)(uint8_t)o[3] << 24;
+          w.y = (uint32_t)(uint8_t)o[4] | (uint32_t)(uint8_t)o[5] << 8 | (uint32_t)(uint8_t)o[6] << 16 |
+                (uint32_t)(uint8_t)o[7] << 24;
+          w.z = (uint32_t)(uint8_t)o[8] | (uint32_t)(uint8_t)o[9] << 8 | (uint32_t)(uint8_t)o[10] << 16 |
+                (uint32_t)(uint8_t)o[11] << 24;
+          w.w = (uint32_t)(uint8_t)o[12] | (uint32_t)(uint8_t)o[13] << 8 | (uint32_t)(uint8_t)o[14] << 16 |
+                (uint32_t)(uint8_t)o[15] << 24;
+          *reinterpret_cast<uint4*>(op) = w;
+        } else {
+          for (int j = 0; j < cnt; ++j) op[j] = (int8_t)o[j];
+        }
+      } else {
+        int16_t* op = reinterpret_cast<int16_t*>(a.out) + (int64_t)r * a.N + nb;
+        if (cnt == 16) {
+          uint4 w0, w1;
+          w0.x = (uint32_t)(uint16_t)o[0] | (uint32_t)(uint16_t)o[1] << 16;
+          w0.y = (uint32_t)(uint16_t)o[2] | (uint32_t)(uint16_t)o[3] << 16;
+          w0.z = (uint32_t)(uint16_t)o[4] | (uint32_t)(uint16_t)o[5] << 16;
+          w0.w = (uint32_t)(uint16_t)o[6] | (uint32_t)(uint16_t)o[7] << 16;
+          w1.x = (uint32_t)(uint16_t)o[8] | (uint32_t)(uint16_t)o[9] << 16;
+          w1.y = (uint32_t)(uint16_t)o[10] | (uint32_t)(uint16_t)o[11] << 16;
+          w1.z = (uint32_t)(uint16_t)o[12] | (uint32_t)(uint16_t)o[13] << 16;
+          w1.w = (uint32_t)(uint16_t)o[14] | (uint32_t)(uint16_t)o[15] << 16;
+          reinterpret_cast<uint4*>(op)[0] = w0;
+          reinterpret_cast<uint4*>(op)[1] = w1;
+        } else {
+          for (int j = 0; j < cnt; ++j) op[j] = (int16_t)o[j];
+        }
+      }
+    }
+  }
+  if (ksplit > 1) cluster_sync();  // peers keep their shared memory until rank 0 has read it
+  // ---- teardown: drain copies issued but never consumed (abort path), free TMEM ----
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && abort_flag) {
+    // wait (bounded) for the last load issued into each stage to land before the CTA exits
+    for (int i = issued - S > 0 ? issued - S : 0; i < issued; ++i) {
+      for (uint32_t it = 0; it < (1u << 22); ++it)
+        if (mbar_try_wait(&full_bar[i % S], (i / S) & 1)) break;
+    }
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(NT < 32 ? 32 : NT));
+  }
+}
+
+}  // namespace tc
+
+// ---------------------------------------------------------------------------------------
+// host side: tensor maps and launch
+// ---------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// int8 row-major matrix [rows][K] -> 2-D tensor map with a (128 B x box_rows) box, 128-byte swizzle
+cudaError_t make_tmap_i8(CUtensorMap* map, const void* base, int64_t rows, int64_t K, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (K & 15) || box_rows < 1 || box_rows > 256)
+    return cudaErrorInvalidValue;
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)K};
+  const cuuint32_t box[2] = {(cuuint32_t)tc::BK, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <int NT, int S>
+static cudaError_t launch_tc_t(const CUtensorMap& ma, const CUtensorMap& mw, const LinearArgs& a, int ksplit,
+                               int32_t* err, cudaStream_t st) {
+  using L = tc::Smem<NT, S>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(tc::k_linear_tc<NT, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(tc::k_linear_tc<NT, S>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.N + NT - 1) / NT, (a.R + tc::BM - 1) / tc::BM * ksplit, 1);
+  cfg.blockDim = dim3(tc::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  int na = 0;
+  if (ksplit > 1) {
+    // cluster spans ksplit CTAs along y; blockIdx.y / ksplit is the row tile
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = ksplit;
+    attr[0].val.clusterDim.z = 1;
+    na = 1;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, tc::k_linear_tc<NT, S>, ma, mw, a, ksplit, err);
+}
+
+cudaError_t prepare_linear_tc() { return encode_fn() ? cudaSuccess : cudaErrorNotSupported; }
+
+cudaError_t launch_linear_tc(const CUtensorMap& map_a, const CUtensorMap& map_w, const LinearArgs& a, int nt,
+                             int ksplit, int32_t* err, cudaStream_t st) {
+  if (a.R <= 0 || a.N <= 0) return cudaSuccess;
+  switch (nt) {
+    case 16: return launch_tc_t<16, 6>(map_a, map_w, a, ksplit, err, st);
+    case 32: return launch_tc_t<32, 6>(map_a, map_w, a, ksplit, err, st);
+    case 64: return launch_tc_t<64, 5>(map_a, map_w, a, ksplit, err, st);
+    case 128: return launch_tc_t<128, 4>(map_a, map_w, a, ksplit, err, st);
+    case 256: return launch_tc_t<256, 3>(map_a, map_w, a, ksplit, err, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace llx

@@ -3,6 +3,7 @@
 // Position-dependent kernels read POS from device memory (`d_pos`) so that a captured
 // CUDA graph replays for any position.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -65,6 +66,15 @@ struct LinearArgs {
 
 // CUDA-core paths: 0 = auto, 1 = GEMV (small R), 2 = tiled dp4a
 cudaError_t launch_linear(const LinearArgs& a, int path, cudaStream_t st);
+
+// Tensor-core path (gemm_tc.cu).  map_a: activations [rows][K] with a 128-row box;
+// map_w: weights [N][K] with an nt-row box; both from make_tmap_i8.  nt in
+// {16, 32, 64, 128, 256}; ksplit CTAs per cluster split K (1 = none).  err receives a
+// nonzero code if a pipeline wait timed out.
+cudaError_t make_tmap_i8(CUtensorMap* map, const void* base, int64_t rows, int64_t K, int box_rows);
+cudaError_t prepare_linear_tc();
+cudaError_t launch_linear_tc(const CUtensorMap& map_a, const CUtensorMap& map_w, const LinearArgs& a, int nt,
+                             int ksplit, int32_t* err, cudaStream_t st);
 
 // ---- attention engine -------------------------------------------------------------------
 struct AttnArgs {

@@ -23,6 +23,7 @@
 #include <sstream>
 #include <stdexcept>
 #include <string>
+#include <tuple>
 #include <unordered_map>
 #include <vector>
 
@@ -116,6 +117,7 @@ struct llx_model {
   size_t blob_bytes = 0;
   uint8_t* d_blob = nullptr;
   uint16_t* d_luts = nullptr;  // numerics.cuh kLut* layout
+  int sms = 148;
 };
 
 namespace llx {
@@ -542,6 +544,13 @@ static void load_model(llx_model* m, const std::string& dir) {
     LLX_CUDA(cudaMalloc(&m->d_luts, sizeof(tab)));
     LLX_CUDA(cudaMemcpy(m->d_luts, tab, sizeof(tab), cudaMemcpyHostToDevice));
   }
+  LLX_CUDA(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, m->device));
+  if (m->opts.gemm_path == 0 || m->opts.gemm_path == 3) {
+    int major = 0;
+    LLX_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, m->device));
+    require(major == 10, LLX_ERR_UNSUPPORTED, "the tensor-core path needs an sm_100 (B200) device");
+    LLX_CUDA(prepare_linear_tc());
+  }
   size_t att_smem = 0;
   for (const Step& x : m->steps)
     if (x.kind == SK::Attention) att_smem = std::max(att_smem, attention_smem_bytes(x.H, x.Hkv, x.D, m->max_seq));
@@ -588,6 +597,10 @@ struct llx_session {
   int32_t* h_pos = nullptr;
   int16_t* h_i16 = nullptr;
   size_t h_i16_n = 0;
+  std::vector<size_t> act_rows;  // allocated rows of each activation buffer
+  size_t tail_rows_alloc = 0;
+  std::map<std::tuple<const void*, int64_t, int64_t, int>, CUtensorMap> tmaps;
+  int32_t* d_fault = nullptr;  // nonzero: a tensor-core pipeline wait timed out
   cudaGraphExec_t decode_exec = nullptr;
   int decode_launches = 0;
   int last_R = 0, last_Rtail = 0;
@@ -600,14 +613,50 @@ static void* dptr(llx_model* m, int64_t off) { return off < 0 ? nullptr : m->d_b
 
 struct Binding {
   std::vector<void*> p;
+  std::vector<size_t> rows;  // allocated rows behind p[i]
 };
 
 static Binding bind(llx_session* s, bool tail_mode) {
   Binding b;
   b.p.resize(s->m->acts.size());
-  for (size_t i = 0; i < s->m->acts.size(); ++i) b.p[i] = s->arena + s->act_off[i];
+  b.rows.resize(s->m->acts.size());
+  for (size_t i = 0; i < s->m->acts.size(); ++i) {
+    b.p[i] = s->arena + s->act_off[i];
+    b.rows[i] = s->act_rows[i];
+  }
   (void)tail_mode;
   return b;
+}
+
+static const CUtensorMap& tmap(llx_session* s, const void* base, int64_t rows, int64_t K, int box) {
+  auto key = std::make_tuple(base, rows, K, box);
+  auto it = s->tmaps.find(key);
+  if (it != s->tmaps.end()) return it->second;
+  CUtensorMap mp;
+  const cudaError_t e = make_tmap_i8(&mp, base, rows, K, box);
+  if (e != cudaSuccess) throw Error(LLX_ERR_CUDA, std::string("tensor map encode failed: ") + cudaGetErrorString(e));
+  return s->tmaps.emplace(key, mp).first->second;
+}
+
+// Tensor-core tiling for R rows x N channels x K: the widest channel tile that still
+// fills the GPU, else the narrowest tile with K split across a cluster.
+static void pick_tc_tiling(int R, int N, int K, int sms, int* nt, int* ksplit) {
+  const int row_tiles = (R + 127) / 128;
+  const int cands[5] = {256, 128, 64, 32, 16};
+  for (int c : cands) {
+    if ((int64_t)((N + c - 1) / c) * row_tiles >= sms) {
+      *nt = c;
+      *ksplit = 1;
+      return;
+    }
+  }
+  *nt = 16;
+  const int ctas = (N + 15) / 16 * row_tiles;
+  const int nkb = (K + 127) / 128;
+  int ks = (sms + ctas - 1) / ctas;
+  ks = std::min(ks, 8);
+  ks = std::min(ks, std::max(1, nkb / 2));
+  *ksplit = std::max(1, ks);
 }
 
 // Enqueue steps [from, to) over R rows (M rows per sequence).
@@ -649,7 +698,17 @@ static int enqueue_steps(llx_session* s, const Binding& bd, size_t from, size_t 
         a.silu_sh = x.silu_sh;
         a.aux_shift = x.aux_shift;
         a.luts = m->d_luts;
-        e = launch_linear(a, m->opts.gemm_path, st);
+        int path = m->opts.gemm_path;
+        if (path == 0) path = R >= 16 ? 3 : 1;
+        if (path == 3) {
+          int nt = 16, ks = 1;
+          pick_tc_tiling(R, x.N, x.K, m->sms, &nt, &ks);
+          const CUtensorMap& ma = tmap(s, a.A, (int64_t)bd.rows[x.in], x.K, 128);
+          const CUtensorMap& mw = tmap(s, a.W, x.N, x.K, nt);
+          e = launch_linear_tc(ma, mw, a, nt, ks, s->d_fault, st);
+        } else {
+          e = launch_linear(a, path, st);
+        }
         break;
       }
       case SK::Rope: {
@@ -759,8 +818,12 @@ static void plan_arena(llx_session* s) {
     for (int a : {m->steps[i].out, m->steps[i].out2})
       if (a >= 0) in_tail[a] = 1;
   std::vector<size_t> bytes(na);
-  for (size_t i = 0; i < na; ++i)
-    bytes[i] = round256((in_tail[i] ? tail_rows : rows) * m->acts[i].cols * m->acts[i].elem);
+  s->act_rows.assign(na, 0);
+  s->tail_rows_alloc = tail_rows;
+  for (size_t i = 0; i < na; ++i) {
+    s->act_rows[i] = in_tail[i] ? tail_rows : rows;
+    bytes[i] = round256(s->act_rows[i] * m->acts[i].cols * m->acts[i].elem);
+  }
   s->act_off.assign(na, 0);
   ArenaPlanner ap;
   if (s->keep) {
@@ -820,11 +883,14 @@ static void ensure_i16(llx_session* s, size_t n) {
 }
 
 static void check_device_error(llx_session* s) {
-  int32_t err = 0;
-  LLX_CUDA(cudaMemcpyAsync(&err, s->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost, s->st));
+  int32_t err[2] = {0, 0};
+  LLX_CUDA(cudaMemcpyAsync(err, s->d_err, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost, s->st));
   LLX_CUDA(cudaStreamSynchronize(s->st));
-  if (err) {
-    LLX_CUDA(cudaMemsetAsync(s->d_err, 0, sizeof(int32_t), s->st));
+  if (err[0] || err[1]) {
+    LLX_CUDA(cudaMemsetAsync(s->d_err, 0, 2 * sizeof(int32_t), s->st));
+    LLX_CUDA(cudaStreamSynchronize(s->st));
+    if (err[1])
+      throw Error(LLX_ERR_DEVICE, "a tensor-core pipeline wait timed out (code " + std::to_string(err[1]) + ")");
     throw Error(LLX_ERR_RANGE, "token ID exceeds model vocabulary");
   }
 }
@@ -876,6 +942,7 @@ static void run_launch(llx_session* s, int M, int pos, bool with_embed, const in
           launch_gather_rows(bd.p[a], dst, s->d_rec, Rtail, m->acts[a].cols * m->acts[a].elem, s->st);
       if (e != cudaSuccess) throw Error(LLX_ERR_CUDA, cudaGetErrorString(e));
       bt.p[a] = dst;
+      bt.rows[a] = s->tail_rows_alloc;
     }
     enqueue_steps(s, bt, m->tail_start, m->steps.size(), Rtail, n_rec);
   }
@@ -970,6 +1037,7 @@ static void session_create(llx_model* m, int batch, int max_rows, int keep, llx_
   LLX_CUDA(cudaMalloc(&s->d_pos, sizeof(int32_t) * 4));
   s->d_step = s->d_pos + 1;
   s->d_err = s->d_pos + 2;
+  s->d_fault = s->d_pos + 3;
   LLX_CUDA(cudaMemset(s->d_pos, 0, sizeof(int32_t) * 4));
   LLX_CUDA(cudaMemset(s->d_tokens, 0, sizeof(int32_t) * rows));
   LLX_CUDA(cudaMallocHost(&s->h_tok, sizeof(int32_t) * rows));

@@ -136,3 +136,47 @@ def build(out: Path, *, dim=64, n_layers=2, H=4, Hkv=2, D=32, ffn=96, vocab=40, 
     (out / "qweights.bin").write_bytes(b"".join(blob.parts))
     (out / "qgraph.json").write_text(json.dumps(g))
     return out
+
+
+def build_linear(out: Path, *, K: int, N: int, epi: str = "none", chain_i8: int = 0, seed: int = 0,
+                 bias: bool = True, max_seq: int = 512) -> Path:
+    """Minimal graph: quant(input) -> [linear i8 out (chain_i8 channels) ->] linear -> logits.
+    epi selects the final linear's epilogue (resadd/mul use `input` as aux, so N == K there)."""
+    rng = np.random.default_rng(seed)
+    blob = _Blob()
+    dim = K
+    blob.add("embed", rng.integers(-20000, 20000, (16, dim)), "i16", -10)
+    blob.add("rope_cos", np.zeros((max_seq, 8), np.int16), "i16")
+    blob.add("rope_sin", np.zeros((max_seq, 8), np.int16), "i16")
+    ops = [{"op": "quant", "in": "input", "out": "input.q", "M": int(rng.integers(1 << 30, 1 << 31)), "S": 37}]
+
+    def lin(a, w, y, n, k, out_dtype, ep, aux=None, aux_shift=0, silu=None):
+        blob.add(w, rng.integers(-128, 128, (n, k)), "i8")
+        lo, hi = (26, 36) if out_dtype == "i16" else (30, 40)
+        blob.add(w + ".rq", np.stack([rng.integers(1 << 30, 1 << 31, n), rng.integers(lo, hi, n)], 1), "rq")
+        b = None
+        if bias:
+            blob.add(w + ".b", rng.integers(-(1 << 20), 1 << 20, n), "i32")
+            b = w + ".b"
+        ops.append({"op": "linear", "in": a, "w": w, "rq": w + ".rq", "bias": b, "out": y, "N": n, "K": k,
+                    "out_dtype": out_dtype, "epilogue": ep, "aux": aux, "aux_shift": aux_shift, "silu": silu})
+
+    src, k = "input.q", K
+    if chain_i8:
+        lin(src, "w0", "mid", chain_i8, K, "i8", "none")
+        src, k = "mid", chain_i8
+    kw = {}
+    if epi in ("resadd", "mul"):
+        assert N == K
+        kw = {"aux": "input", "aux_shift": 15 if epi == "mul" else 0}
+    if epi == "silu":
+        kw = {"silu": {"Mi": 1 << 30, "Si": 30, "sh_out": 16}}
+    lin(src, "w1", "logits", N, k, "i16", epi, **kw)
+    g = {"model": {"dim": dim, "n_layers": 0, "n_heads": 1, "n_kv_heads": 1, "head_dim": 16, "ffn": 16,
+                   "vocab": min(16, N), "vocab_padded": N, "max_seq": max_seq, "E_RES": -10, "E_LOGIT": -6},
+         "weights_file": "qweights.bin", "tensors": blob.tensors, "ops": ops, "input": "input", "output": "logits"}
+    out = Path(out)
+    out.mkdir(parents=True, exist_ok=True)
+    (out / "qweights.bin").write_bytes(b"".join(blob.parts))
+    (out / "qgraph.json").write_text(json.dumps(g))
+    return out
