@@ -656,7 +656,9 @@ static void pick_tc_tiling(int R, int N, int K, int sms, int* nt, int* ksplit) {
   int ks = (sms + ctas - 1) / ctas;
   ks = std::min(ks, 8);
   ks = std::min(ks, std::max(1, nkb / 2));
-  *ksplit = std::max(1, ks);
+  int p2 = 1;
+  while (p2 * 2 <= ks) p2 *= 2;  // cluster sizes 1, 2, 4, 8
+  *ksplit = p2;
 }
 
 // Enqueue steps [from, to) over R rows (M rows per sequence).
