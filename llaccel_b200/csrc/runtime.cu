@@ -1013,7 +1013,9 @@ static void session_create(llx_model* m, int batch, int max_rows, int keep, llx_
   s->B = batch;
   s->max_rows = max_rows;
   s->keep = keep != 0;
-  s->max_tail_rows = std::min(max_rows, 64);
+  // the row-independent tail (final norm, lm_head, ...) holds every row of a launch when
+  // that costs at most 2 GB of logits, else 64 recorded rows per sequence
+  s->max_tail_rows = (double)batch * max_rows * m->vocab_padded * 2.0 <= 2.0e9 ? max_rows : std::min(max_rows, 64);
   LLX_CUDA(cudaSetDevice(m->device));
   LLX_CUDA(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
   plan_arena(s);
