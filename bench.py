@@ -269,6 +269,22 @@ def _has_cuda() -> bool:
         return False
 
 
+def _by_kind(prof: list[dict]) -> dict:
+    """Per-step kernel time summed by kind (linear steps split by output role)."""
+    out: dict[str, list] = {}
+    for p in prof:
+        kind, _, name = p["label"].partition(":")
+        if kind == "linear":
+            role = name.split(".")[-1] if "." in name else name
+            kind = f"linear.{role}"
+        e = out.setdefault(kind, [0, 0.0, 0.0])
+        e[0] += 1
+        e[1] += p["ms"]
+        e[2] += p["bytes"]
+    return {k: {"n": v[0], "ms": round(v[1], 4), "GBs": round(v[2] / max(v[1], 1e-9) / 1e6, 1)}
+            for k, v in sorted(out.items(), key=lambda kv: -kv[1][1])}
+
+
 def run_ours(args, dist: Dist) -> None:
     import torch
     from llaccel_b200 import build
@@ -382,8 +398,9 @@ def run_ours(args, dist: Dist) -> None:
         "clocks": clock,
         "gpu_launches": launches_per_step * n_dec * args.steps,
         "determinism": deterministic,
-        "profile": [{"k": p["label"], "ms": round(p["ms"], 5), "GBs": round(p["bytes"] / max(p["ms"], 1e-9) / 1e6, 1)}
-                    for p in sorted(prof, key=lambda p: -p["ms"])[:12]],
+        "profile_by_kind": _by_kind(prof),
+        "profile_top": [{"k": p["label"], "ms": round(p["ms"], 5), "GBs": round(p["bytes"] / max(p["ms"], 1e-9) / 1e6, 1)}
+                        for p in sorted(prof, key=lambda p: -p["ms"])[:6]],
     }
     if dist.rank == 0:
         print(json.dumps(line), flush=True)

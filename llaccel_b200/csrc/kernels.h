@@ -94,5 +94,6 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st);
 // opt the attention kernel into `smem` bytes of dynamic shared memory (once per device, before capture)
 cudaError_t prepare_attention(size_t smem);
 size_t attention_smem_bytes(int H, int Hkv, int D, int T);
+size_t attention_decode_smem_bytes(int H, int Hkv, int D, int max_seq);
 
 }  // namespace llx

@@ -118,13 +118,214 @@ __global__ void k_attention(const int8_t* __restrict__ q, const int8_t* __restri
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// Decode attention (one query row per sequence): one CTA per (sequence, KV head) streams
+// the key rows, then the value rows, with 16-byte loads.  LPK = D/16 lanes share one key
+// row; the H/Hkv query heads of the KV head reuse every loaded row.  Per-head max / sum /
+// normalisation run one warp per head over the scores kept in shared memory; the value
+// pass accumulates RB heads at a time in registers, reduces across lanes with shuffles and
+// across warps through shared memory.  All reductions are integer: exact in any order.
+// ---------------------------------------------------------------------------------------
+constexpr int kDecThreads = 256, kDecWarps = kDecThreads / 32;
+
+size_t attention_decode_smem_bytes(int H, int Hkv, int D, int max_seq) {
+  const int rep = H / Hkv;
+  return (size_t)rep * max_seq * 4 + (size_t)kDecWarps * rep * D * 4 + (size_t)rep * D + 64;
+}
+
+__device__ __forceinline__ int dot16_i8(const uint4& a, const uint4& b, int acc) {
+  acc = __dp4a((int)a.x, (int)b.x, acc);
+  acc = __dp4a((int)a.y, (int)b.y, acc);
+  acc = __dp4a((int)a.z, (int)b.z, acc);
+  acc = __dp4a((int)a.w, (int)b.w, acc);
+  return acc;
+}
+
+template <int LPK, int RB>
+__global__ void __launch_bounds__(kDecThreads) k_attention_decode(
+    const int8_t* __restrict__ q, const int8_t* __restrict__ kc, const int8_t* __restrict__ vc, int8_t* __restrict__ out,
+    int H, int Hkv, int max_seq, const int* __restrict__ d_pos, int64_t Ms, int Ss, int64_t Mo, int So, int prob_bits,
+    const uint16_t* __restrict__ luts) {
+  constexpr int D = LPK * 16;
+  constexpr int KPW = 32 / LPK;  // keys per warp per iteration
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ uint16_t s_expi[16], s_expf[256];
+  const int rep = H / Hkv;
+  int32_t* sc = reinterpret_cast<int32_t*>(smem);                       // [rep][max_seq]
+  int32_t* red = sc + (size_t)rep * max_seq;                             // [warps][rep][D]
+  int8_t* q_s = reinterpret_cast<int8_t*>(red + (size_t)kDecWarps * rep * D);  // [rep][D]
+  const int b = blockIdx.x, kvh = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane % LPK, kg = lane / LPK;
+  const int T = *d_pos + 1;
+
+  for (int i = threadIdx.x; i < 16 + 256; i += blockDim.x) {
+    if (i < 16)
+      s_expi[i] = luts[kLutExpI + i];
+    else
+      s_expf[i - 16] = luts[kLutExpF + i - 16];
+  }
+  const int8_t* qrow = q + ((int64_t)b * H + (int64_t)kvh * rep) * D;
+  for (int i = threadIdx.x; i < rep * D / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(q_s)[i] = reinterpret_cast<const uint4*>(qrow)[i];
+  __syncthreads();
+
+  const int8_t* kbase = kc + ((int64_t)b * Hkv + kvh) * max_seq * D;
+  const int8_t* vbase = vc + ((int64_t)b * Hkv + kvh) * max_seq * D;
+  const int stride = kDecWarps * KPW;
+
+  // ---- scores ----
+  for (int t0 = warp * KPW; t0 < T; t0 += 2 * stride) {
+    const int ta = t0 + kg, tb = t0 + stride + kg;
+    uint4 ka = make_uint4(0, 0, 0, 0), kb = make_uint4(0, 0, 0, 0);
+    if (ta < T) ka = __ldg(reinterpret_cast<const uint4*>(kbase + (int64_t)ta * D) + sub);
+    if (tb < T) kb = __ldg(reinterpret_cast<const uint4*>(kbase + (int64_t)tb * D) + sub);
+    for (int j = 0; j < rep; ++j) {
+      const uint4 qv = reinterpret_cast<const uint4*>(q_s + j * D)[sub];
+      int sa = dot16_i8(ka, qv, 0), sb = dot16_i8(kb, qv, 0);
+#pragma unroll
+      for (int o = 1; o < LPK; o <<= 1) {
+        sa += __shfl_xor_sync(0xffffffffu, sa, o);
+        sb += __shfl_xor_sync(0xffffffffu, sb, o);
+      }
+      if (sub == 0) {
+        if (ta < T) sc[j * max_seq + ta] = sa;
+        if (tb < T) sc[j * max_seq + tb] = sb;
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- max, exp-sum, normalised probabilities: one warp per head ----
+  const int pmax = (1 << prob_bits) - 1, pshift = 31 - prob_bits;
+  for (int j = warp; j < rep; j += kDecWarps) {
+    int32_t* s = sc + j * max_seq;
+    int32_t mx = INT_MIN;
+    for (int t = lane; t < T; t += 32) mx = max(mx, s[t]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    uint32_t sum = 0;
+    for (int t = lane; t < T; t += 32) {
+      const uint32_t p = exp_prob(mulshift((int64_t)mx - s[t], Ms, Ss), s_expi, s_expf);
+      s[t] = (int32_t)p;
+      sum += p;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const int64_t inv = udiv((uint64_t)1 << 31, sum);
+    for (int t = lane; t < T; t += 32) {
+      const int64_t pn = rshr((int64_t)s[t] * inv, pshift);
+      s[t] = (int32_t)(pn < pmax ? pn : pmax);
+    }
+  }
+  __syncthreads();
+
+  // ---- o[j][d] = sum_t pn[j][t] * v[t][d], RB heads per pass ----
+  int8_t* orow = out + ((int64_t)b * H + (int64_t)kvh * rep) * D;
+  for (int j0 = 0; j0 < rep; j0 += RB) {
+    int32_t acc[RB][16];
+#pragma unroll
+    for (int r = 0; r < RB; ++r)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[r][i] = 0;
+    for (int t = warp * KPW + kg; t < T; t += stride) {
+      const uint4 vv = __ldg(reinterpret_cast<const uint4*>(vbase + (int64_t)t * D) + sub);
+      const uint32_t w[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+        const int j = j0 + r;
+        const int32_t pn = j < rep ? sc[j * max_seq + t] : 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[r][i] += pn * (int32_t)(int8_t)(w[i >> 2] >> (8 * (i & 3)));
+      }
+    }
+    // lanes holding the same d chunk (same sub) but different keys
+#pragma unroll
+    for (int o = LPK; o < 32; o <<= 1)
+#pragma unroll
+      for (int r = 0; r < RB; ++r)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[r][i] += __shfl_xor_sync(0xffffffffu, acc[r][i], o);
+    if (kg == 0) {
+#pragma unroll
+      for (int r = 0; r < RB; ++r)
+        if (j0 + r < rep)
+#pragma unroll
+          for (int i = 0; i < 16; ++i) red[((size_t)warp * rep + j0 + r) * D + sub * 16 + i] = acc[r][i];
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < RB * D; idx += blockDim.x) {
+      const int j = j0 + idx / D, d = idx % D;
+      if (j >= rep) continue;
+      int32_t o = 0;
+#pragma unroll
+      for (int w = 0; w < kDecWarps; ++w) o += red[((size_t)w * rep + j) * D + d];
+      int64_t ov = o;
+      if (prob_bits == 15) ov = rshr(ov, 7);
+      orow[j * D + d] = (int8_t)sat8(mulshift(ov, Mo, So));
+    }
+    __syncthreads();
+  }
+}
+
+template <int LPK>
+static cudaError_t launch_dec_l(const AttnArgs& a, size_t smem, cudaStream_t st) {
+  const int rep = a.H / a.Hkv;
+  dim3 grid(a.B, a.Hkv);
+  if (rep >= 8) {
+    k_attention_decode<LPK, 8><<<grid, kDecThreads, smem, st>>>(a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos,
+                                                               a.Ms, a.Ss, a.Mo, a.So, a.prob_bits, a.luts);
+  } else if (rep >= 4) {
+    k_attention_decode<LPK, 4><<<grid, kDecThreads, smem, st>>>(a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos,
+                                                               a.Ms, a.Ss, a.Mo, a.So, a.prob_bits, a.luts);
+  } else if (rep >= 2) {
+    k_attention_decode<LPK, 2><<<grid, kDecThreads, smem, st>>>(a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos,
+                                                               a.Ms, a.Ss, a.Mo, a.So, a.prob_bits, a.luts);
+  } else {
+    k_attention_decode<LPK, 1><<<grid, kDecThreads, smem, st>>>(a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos,
+                                                               a.Ms, a.Ss, a.Mo, a.So, a.prob_bits, a.luts);
+  }
+  return cudaGetLastError();
+}
+
+template <int LPK>
+static cudaError_t prep_dec_l(size_t smem) {
+  for (auto f : {k_attention_decode<LPK, 1>, k_attention_decode<LPK, 2>, k_attention_decode<LPK, 4>,
+                 k_attention_decode<LPK, 8>}) {
+    const cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
 cudaError_t prepare_attention(size_t smem) {
-  return cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  for (auto f : {prep_dec_l<1>, prep_dec_l<2>, prep_dec_l<4>, prep_dec_l<8>, prep_dec_l<16>}) {
+    e = f(smem);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t st) {
+  if (a.B <= 0) return cudaSuccess;
+  const size_t smem = attention_decode_smem_bytes(a.H, a.Hkv, a.D, a.max_seq);
+  switch (a.D) {
+    case 16: return launch_dec_l<1>(a, smem, st);
+    case 32: return launch_dec_l<2>(a, smem, st);
+    case 64: return launch_dec_l<4>(a, smem, st);
+    case 128: return launch_dec_l<8>(a, smem, st);
+    case 256: return launch_dec_l<16>(a, smem, st);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st) {
   const int R = a.B * a.M;
   if (R <= 0) return cudaSuccess;
+  if (a.M == 1 && (a.D == 16 || a.D == 32 || a.D == 64 || a.D == 128 || a.D == 256))
+    return launch_attention_decode(a, st);
   const size_t smem = attention_smem_bytes(a.H, a.Hkv, a.D, a.max_seq);
   dim3 grid(R, a.Hkv);
   k_attention<<<grid, 256, smem, st>>>(a.q, a.kc, a.vc, a.out, a.M, a.H, a.Hkv, a.D, a.max_seq, a.d_pos, a.Ms, a.Ss,

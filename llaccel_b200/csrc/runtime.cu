@@ -553,7 +553,9 @@ static void load_model(llx_model* m, const std::string& dir) {
   }
   size_t att_smem = 0;
   for (const Step& x : m->steps)
-    if (x.kind == SK::Attention) att_smem = std::max(att_smem, attention_smem_bytes(x.H, x.Hkv, x.D, m->max_seq));
+    if (x.kind == SK::Attention)
+      att_smem = std::max({att_smem, attention_smem_bytes(x.H, x.Hkv, x.D, m->max_seq),
+                           attention_decode_smem_bytes(x.H, x.Hkv, x.D, m->max_seq)});
   if (att_smem) {
     int optin = 0;
     LLX_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device));
