@@ -7,9 +7,9 @@
 //           weight tile [NT x 128 B] (both K-major, 128-byte swizzle) into stage s;
 //   warp 1  allocates NT TMEM columns, one thread issues 4 MMAs (K = 32 each) per block
 //           and commits each stage back to the producer, then the accumulator;
-//   warps 2-5 read the int32 accumulator rows from TMEM (one row per thread), add the
-//           bias, requantize per channel, apply the epilogue and store 16 channels at a
-//           time (i16 or i8), row-major.
+//   warps 2-9 read the int32 accumulator rows from TMEM (one row per thread; two warps
+//           per TMEM lane quarter split the channel chunks), add the bias, requantize per
+//           channel, apply the epilogue and store 16 channels at a time (i16 or i8).
 // The int32 accumulation is exact (|acc| <= K * 2^14 < 2^31 for K < 2^17), so the tensor
 // core result equals the reference's int64 matmul.  Rows and K past the tensor extents
 // are zero-filled by TMA.  Every mbarrier wait is bounded: on timeout the CTA records an
@@ -33,7 +33,7 @@ namespace tc {
 
 constexpr int BM = 128;         // MMA M: activation rows per tile
 constexpr int BK = 128;         // bytes of K per stage (= the 128-byte swizzle span)
-constexpr int kThreads = 192;   // 6 warps
+constexpr int kThreads = 320;   // 10 warps: TMA, MMA, 8 epilogue
 constexpr uint32_t kSpinLimit = 1u << 26;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -132,17 +132,33 @@ __device__ __forceinline__ uint32_t dsmem_ld(const void* local, uint32_t rank) {
   return v;
 }
 
-__device__ __forceinline__ int64_t epi_value(int32_t acc, int64_t bias, int64_t M, int S, int64_t aux,
-                                             const LinearArgs& a) {
-  const int64_t v = (int64_t)acc + bias;
-  if (a.out_i8) return sat8(mulshift(v, M, S));
-  const int64_t t = sat16(mulshift(v, M, S));
-  switch (a.epi) {
-    case EPI_RESADD: return sat16(t + aux);
-    case EPI_SILU: return silu16(t, a.silu_Mi, a.silu_Si, a.silu_sh, a.luts + kLutSig);
-    case EPI_MUL: return sat16(rshr(t * aux, a.aux_shift));
-    default: return t;
-  }
+__device__ __forceinline__ int64_t rshr64(int64_t v, int s) { return s == 0 ? v : (v >> s) + ((v >> (s - 1)) & 1); }
+__device__ __forceinline__ int32_t sat16_64(int64_t v) { return (int32_t)(v < -32768 ? -32768 : (v > 32767 ? 32767 : v)); }
+__device__ __forceinline__ int32_t sat8_64(int64_t v) { return (int32_t)(v < -128 ? -128 : (v > 127 ? 127 : v)); }
+__device__ __forceinline__ int32_t sat16_32(int32_t v) { return v < -32768 ? -32768 : (v > 32767 ? 32767 : v); }
+// rshr of a value with |v| < 2^31: 32-bit arithmetic for s < 31, 64-bit otherwise
+__device__ __forceinline__ int32_t rshr_small(int32_t v, int s) {
+  if (s == 0) return v;
+  if (s < 31) return (v >> s) + ((v >> (s - 1)) & 1);
+  return (int32_t)rshr64(v, s);
+}
+
+// Per-channel requant of an int32 accumulator (NUMERICS.md:69-71): v = acc + bias in 64 bits
+// (or 32 when the host proved |acc + bias| < 2^31), times M (< 2^32) in 64 bits, rshr S.
+__device__ __forceinline__ int64_t requant64(int32_t acc, int64_t bias, uint32_t M, int S, bool narrow) {
+  const int64_t v = narrow ? (int64_t)(int32_t)(acc + (int32_t)bias) : (int64_t)acc + bias;
+  return rshr64(narrow ? (int64_t)(int32_t)v * (int64_t)M : (int64_t)((uint64_t)v * (uint64_t)M), S);
+}
+
+// SiLU of an i16 value with the sigmoid table in shared memory (numerics.h:45-51).  Every
+// intermediate after the input scaling fits 32 bits: |x * sg| <= 2^15 * 65514 < 2^31.
+__device__ __forceinline__ int32_t silu_fast(int32_t x, uint32_t Mi, int Si, int sh_out, const uint16_t* sig) {
+  const int32_t u = sat16_64(rshr64((int64_t)x * (int64_t)Mi, Si));
+  const int idx = (u >> 8) + 128;
+  const int32_t f = u & 255;
+  const int32_t lo = sig[idx];
+  const int32_t sg = lo + (((int32_t)sig[idx + 1] - lo) * f >> 8);
+  return sat16_32(rshr_small(x * sg, sh_out));
 }
 
 template <int NT, int S>
@@ -157,7 +173,7 @@ struct Smem {
 };
 
 template <int NT, int S>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     k_linear_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w, LinearArgs a,
                 int ksplit, int32_t* err) {
   using L = Smem<NT, S>;
@@ -167,8 +183,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
   __shared__ int issued;  // TMA stages issued by the producer
-  __shared__ int64_t s_M[NT], s_bias[NT];
+  __shared__ int64_t s_bias[NT];
+  __shared__ uint32_t s_M[NT];
   __shared__ int s_S[NT];
+  __shared__ uint16_t s_sig[260];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * NT;
@@ -199,10 +217,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   // per-channel requant parameters
   for (int i = threadIdx.x; i < NT; i += blockDim.x) {
     const int n = n0 + i;
-    s_M[i] = n < a.N ? (int64_t)a.rq[2 * n] : 0;
+    s_M[i] = n < a.N ? (uint32_t)a.rq[2 * n] : 0u;
     s_S[i] = n < a.N ? a.rq[2 * n + 1] : 0;
     s_bias[i] = (n < a.N && a.bias) ? (int64_t)a.bias[n] : 0;
   }
+  if (a.epi == EPI_SILU)
+    for (int i = threadIdx.x; i < 257; i += blockDim.x) s_sig[i] = a.luts[kLutSig + i];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -252,8 +272,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(&acc_bar);  // fires once every MMA issued above has completed (or at once if none)
     }
   } else {
-    // ---- epilogue warps 2..5: TMEM lane quarter = warp % 4 ----
+    // ---- epilogue warps 2..9: TMEM lane quarter = warp % 4, chunk parity = (warp - 2) / 4 ----
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row_in_tile = q * 32 + lane;
     const bool ok = mbar_wait(&acc_bar, 0, &abort_flag);
     if (!ok) {
@@ -264,8 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int32_t* part = reinterpret_cast<int32_t*>(ring);  // [BM][NT] partials when ksplit > 1
     if (ok && ksplit > 1) {
       // all MMAs are complete, so the ring is free: stage this CTA's partial tile
-#pragma unroll
-      for (int c0 = 0; c0 < NT; c0 += 16) {
+      for (int c0 = half * 16; c0 < NT; c0 += 32) {
         uint32_t v[16];
         tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + c0, v);
         if (nkb == 0) {
@@ -283,11 +303,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp >= 2 && !abort_flag && (ksplit == 1 || crank == 0)) {
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row_in_tile = q * 32 + lane;
     const int r = m0 + row_in_tile;
-    int32_t* part = reinterpret_cast<int32_t*>(ring);
+    const int32_t* part = reinterpret_cast<const int32_t*>(ring);
+    const bool narrow = a.narrow != 0;
 #pragma unroll 1
-    for (int c0 = 0; c0 < NT; c0 += 16) {
+    for (int c0 = half * 16; c0 < NT; c0 += 32) {
       int32_t acc[16];
       if (ksplit == 1) {
         uint32_t v[16];
@@ -303,20 +325,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (r >= a.R) continue;
       const int nb = n0 + c0;
-      if (nb >= a.N) continue;  // N is a multiple of 8; tiles of 16 may straddle only at 8
+      if (nb >= a.N) continue;
       const int cnt = min(16, a.N - nb);
-      int64_t aux[16];
-      if (a.epi == EPI_RESADD || a.epi == EPI_MUL) {
-        const int16_t* ap = a.aux + (int64_t)r * a.N + nb;
+      int32_t o[16];
+      if (a.out_i8) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) aux[j] = j < cnt ? ap[j] : 0;
+        for (int j = 0; j < 16; ++j) o[j] = sat8_64(requant64(acc[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], narrow));
       } else {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) aux[j] = 0;
-      }
-      int32_t o[16];
+        for (int j = 0; j < 16; ++j) o[j] = sat16_64(requant64(acc[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], narrow));
+        if (a.epi == EPI_RESADD || a.epi == EPI_MUL) {
+          int32_t aux[16];
+          const int16_t* ap = a.aux + (int64_t)r * a.N + nb;
+          if (cnt == 16) {
+            const uint4 u0 = reinterpret_cast<const uint4*>(ap)[0], u1 = reinterpret_cast<const uint4*>(ap)[1];
+            const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
-      for (int j = 0; j < 16; ++j) o[j] = (int32_t)epi_value(acc[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], aux[j], a);
+            for (int j = 0; j < 8; ++j) {
+              aux[2 * j] = (int16_t)(w[j] & 0xFFFF);
+              aux[2 * j + 1] = (int16_t)(w[j] >> 16);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) aux[j] = j < cnt ? ap[j] : 0;
+          }
+          if (a.epi == EPI_RESADD) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) o[j] = sat16_32(o[j] + aux[j]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) o[j] = sat16_32(rshr_small(o[j] * aux[j], a.aux_shift));
+          }
+        } else if (a.epi == EPI_SILU) {
+          const uint32_t Mi = (uint32_t)a.silu_Mi;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] = silu_fast(o[j], Mi, a.silu_Si, a.silu_sh, s_sig);
+        }
+      }
       if (a.out_i8) {
         int8_t* op = reinterpret_cast<int8_t*>(a.out) + (int64_t)r * a.N + nb;
         if (cnt == 16) {
@@ -448,9 +493,9 @@ cudaError_t launch_linear_tc(const CUtensorMap& map_a, const CUtensorMap& map_w,
                              int ksplit, int32_t* err, cudaStream_t st) {
   if (a.R <= 0 || a.N <= 0) return cudaSuccess;
   switch (nt) {
-    case 16: return launch_tc_t<16, 6>(map_a, map_w, a, ksplit, err, st);
-    case 32: return launch_tc_t<32, 6>(map_a, map_w, a, ksplit, err, st);
-    case 64: return launch_tc_t<64, 5>(map_a, map_w, a, ksplit, err, st);
+    case 16: return launch_tc_t<16, 4>(map_a, map_w, a, ksplit, err, st);
+    case 32: return launch_tc_t<32, 4>(map_a, map_w, a, ksplit, err, st);
+    case 64: return launch_tc_t<64, 4>(map_a, map_w, a, ksplit, err, st);
     case 128: return launch_tc_t<128, 4>(map_a, map_w, a, ksplit, err, st);
     case 256: return launch_tc_t<256, 3>(map_a, map_w, a, ksplit, err, st);
     default: return cudaErrorInvalidValue;

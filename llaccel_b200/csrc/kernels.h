@@ -62,6 +62,7 @@ struct LinearArgs {
   int silu_Si, silu_sh;
   int aux_shift;
   const uint16_t* luts;  // device tables (SILU epilogue)
+  int narrow;            // 1: |acc + bias| < 2^31 for every channel (proved at load), 32-bit bias add
 };
 
 // CUDA-core paths: 0 = auto, 1 = GEMV (small R), 2 = tiled dp4a

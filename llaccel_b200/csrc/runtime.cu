@@ -77,6 +77,7 @@ struct Step {
   SK kind;
   int in = -1, in2 = -1, out = -1, out2 = -1;  // activation ids
   int64_t w_off = -1, rq_off = -1, bias_off = -1, gamma_off = -1;
+  int narrow = 0;  // linear: |acc + bias| < 2^31 always
   int N = 0, K = 0, heads = 1, H = 0, Hkv = 0, D = 0, layer = -1;
   int out_i8 = 0, epi = 0, aux_shift = 0, silu_Si = 0, silu_sh = 0;
   int64_t silu_Mi = 0;
@@ -336,11 +337,16 @@ static void build_plan(llx_model* m, const json::Value& g, const std::vector<uin
       s.w_off = w.offset;
       s.rq_off = rq.offset;
       const std::string bias = sval_or(op, "bias", "");
+      int64_t max_bias = 0;
       if (!bias.empty()) {
         const TensorSpec& b = tensor(m, bias, DT::I32, ctx);
         require(b.count == s.N, LLX_ERR_INVALID, ctx + ": bias size != N");
         s.bias_off = b.offset;
+        const int32_t* bp = reinterpret_cast<const int32_t*>(blob.data() + b.offset);
+        for (int64_t n = 0; n < b.count; ++n) max_bias = std::max<int64_t>(max_bias, std::llabs((long long)bp[n]));
       }
+      // |sum_k a*w| <= K * 128 * 128; the bias add stays in 32 bits when the total cannot wrap
+      s.narrow = (int64_t)s.K * 16384 + max_bias < (1ll << 31) ? 1 : 0;
       const std::string od = sval_or(op, "out_dtype", "i16");
       const std::string ep = sval_or(op, "epilogue", "none");
       require(od == "i16" || od == "i8", LLX_ERR_INVALID, ctx + ": unknown out_dtype " + od);
@@ -702,6 +708,7 @@ static int enqueue_steps(llx_session* s, const Binding& bd, size_t from, size_t 
         a.silu_sh = x.silu_sh;
         a.aux_shift = x.aux_shift;
         a.luts = m->d_luts;
+        a.narrow = x.narrow;
         int path = m->opts.gemm_path;
         if (path == 0) path = R >= 16 ? 3 : 1;
         if (path == 3) {
