@@ -53,6 +53,7 @@ typedef struct {
   int device;    /* CUDA device ordinal */
   int fuse;      /* 1: fuse QUANT/KV_WRITE into their producers (default); 0: one kernel per op */
   int gemm_path; /* 0 auto, 1 CUDA-core GEMV, 2 CUDA-core tiled, 3 tensor-core tcgen05 */
+  int pdl;       /* 1: programmatic dependent launch between the kernels of a launch (default) */
 } llx_opts;
 
 typedef struct {

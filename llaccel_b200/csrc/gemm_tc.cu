@@ -25,6 +25,7 @@
 #include <cstdint>
 
 #include "kernels.h"
+#include "launch.cuh"
 #include "numerics.cuh"
 
 namespace llx {
@@ -227,11 +228,27 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base;
+  // dependents may launch only once every CTA of this grid holds its TMEM columns, so a
+  // waiting dependent CTA can never keep a CTA of this grid from allocating
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
       // ---- TMA producer ----
-      for (int i = 0; i < nkb; ++i) {
+      // weights are model constants: the first S stages' weight tiles are requested before
+      // the grid dependency wait, overlapping the previous kernel; activations after it
+      const int pre = nkb < S ? nkb : S;
+      for (int i = 0; i < pre; ++i) {
+        uint8_t* sb = ring + i * L::kStage + L::kA;
+        mbar_expect_tx(&full_bar[i], L::kA + L::kB);
+        tma_load_2d(sb, &map_w, &full_bar[i], (kb0 + i) * BK, n0);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) {
+        tma_load_2d(ring + i * L::kStage, &map_a, &full_bar[i], (kb0 + i) * BK, m0);
+        issued = i + 1;
+      }
+      for (int i = pre; i < nkb; ++i) {
         const int s = i % S;
         if (!mbar_wait(&empty_bar[s], ((i / S) + 1) & 1, &abort_flag)) {
           abort_flag = 1;
@@ -246,8 +263,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         tma_load_2d(sb, &map_w, &full_bar[s], kx, n0);
         issued = i + 1;
       }
+    } else {
+      pdl_wait();
     }
   } else if (warp == 1) {
+    pdl_wait();
     if (lane == 0) {
       // ---- MMA issuer ----
       const uint32_t idesc = idesc_i8(NT);
@@ -272,6 +292,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mma_commit(&acc_bar);  // fires once every MMA issued above has completed (or at once if none)
     }
   } else {
+    pdl_wait();  // aux rows and the output buffer belong to earlier kernels
     // ---- epilogue warps 2..9: TMEM lane quarter = warp % 4, chunk parity = (warp - 2) / 4 ----
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
@@ -472,15 +493,18 @@ static cudaError_t launch_tc_t(const CUtensorMap& ma, const CUtensorMap& mw, con
   cfg.blockDim = dim3(tc::kThreads, 1, 1);
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   int na = 0;
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[na].val.programmaticStreamSerializationAllowed = g_pdl ? 1 : 0;
+  ++na;
   if (ksplit > 1) {
     // cluster spans ksplit CTAs along y; blockIdx.y / ksplit is the row tile
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = ksplit;
-    attr[0].val.clusterDim.z = 1;
-    na = 1;
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = ksplit;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;

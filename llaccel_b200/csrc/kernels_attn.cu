@@ -13,6 +13,7 @@
 #include <cstdint>
 
 #include "kernels.h"
+#include "launch.cuh"
 #include "numerics.cuh"
 
 namespace llx {
@@ -41,6 +42,8 @@ __global__ void k_attention(const int8_t* __restrict__ q, const int8_t* __restri
                             int8_t* __restrict__ out, int M, int H, int Hkv, int D, int max_seq,
                             const int* __restrict__ d_pos, int64_t Ms, int Ss, int64_t Mo, int So, int prob_bits,
                             const uint16_t* __restrict__ luts) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ uint16_t s_expi[16], s_expf[256];
   for (int i = threadIdx.x; i < 16 + 256; i += blockDim.x) {
@@ -157,14 +160,15 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   const int b = blockIdx.x, kvh = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane % LPK, kg = lane / LPK;
-  const int T = *d_pos + 1;
-
+  pdl_trigger();
   for (int i = threadIdx.x; i < 16 + 256; i += blockDim.x) {
     if (i < 16)
       s_expi[i] = luts[kLutExpI + i];
     else
       s_expf[i - 16] = luts[kLutExpF + i - 16];
   }
+  pdl_wait();  // POS, q and the KV cache come from earlier kernels
+  const int T = *d_pos + 1;
   const int8_t* qrow = q + ((int64_t)b * H + (int64_t)kvh * rep) * D;
   for (int i = threadIdx.x; i < rep * D / 16; i += blockDim.x)
     reinterpret_cast<uint4*>(q_s)[i] = reinterpret_cast<const uint4*>(qrow)[i];
@@ -273,17 +277,17 @@ static cudaError_t launch_dec_l(const AttnArgs& a, size_t smem, cudaStream_t st)
   const int rep = a.H / a.Hkv;
   dim3 grid(a.B, a.Hkv);
   if (rep >= 8) {
-    k_attention_decode<LPK, 8><<<grid, kDecThreads, smem, st>>>(a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos,
-                                                               a.Ms, a.Ss, a.Mo, a.So, a.prob_bits, a.luts);
+    { const cudaError_t e_ = launch_k(k_attention_decode<LPK, 8>, dim3(grid), dim3(kDecThreads), smem, st, a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos,
+                                                               a.Ms, a.Ss, a.Mo, a.So, a.prob_bits, a.luts); if (e_ != cudaSuccess) return e_; }
   } else if (rep >= 4) {
-    k_attention_decode<LPK, 4><<<grid, kDecThreads, smem, st>>>(a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos,
-                                                               a.Ms, a.Ss, a.Mo, a.So, a.prob_bits, a.luts);
+    { const cudaError_t e_ = launch_k(k_attention_decode<LPK, 4>, dim3(grid), dim3(kDecThreads), smem, st, a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos,
+                                                               a.Ms, a.Ss, a.Mo, a.So, a.prob_bits, a.luts); if (e_ != cudaSuccess) return e_; }
   } else if (rep >= 2) {
-    k_attention_decode<LPK, 2><<<grid, kDecThreads, smem, st>>>(a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos,
-                                                               a.Ms, a.Ss, a.Mo, a.So, a.prob_bits, a.luts);
+    { const cudaError_t e_ = launch_k(k_attention_decode<LPK, 2>, dim3(grid), dim3(kDecThreads), smem, st, a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos,
+                                                               a.Ms, a.Ss, a.Mo, a.So, a.prob_bits, a.luts); if (e_ != cudaSuccess) return e_; }
   } else {
-    k_attention_decode<LPK, 1><<<grid, kDecThreads, smem, st>>>(a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos,
-                                                               a.Ms, a.Ss, a.Mo, a.So, a.prob_bits, a.luts);
+    { const cudaError_t e_ = launch_k(k_attention_decode<LPK, 1>, dim3(grid), dim3(kDecThreads), smem, st, a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos,
+                                                               a.Ms, a.Ss, a.Mo, a.So, a.prob_bits, a.luts); if (e_ != cudaSuccess) return e_; }
   }
   return cudaGetLastError();
 }
@@ -328,8 +332,8 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st) {
     return launch_attention_decode(a, st);
   const size_t smem = attention_smem_bytes(a.H, a.Hkv, a.D, a.max_seq);
   dim3 grid(R, a.Hkv);
-  k_attention<<<grid, 256, smem, st>>>(a.q, a.kc, a.vc, a.out, a.M, a.H, a.Hkv, a.D, a.max_seq, a.d_pos, a.Ms, a.Ss,
-                                        a.Mo, a.So, a.prob_bits, a.luts);
+  { const cudaError_t e_ = launch_k(k_attention, dim3(grid), dim3(256), smem, st, a.q, a.kc, a.vc, a.out, a.M, a.H, a.Hkv, a.D, a.max_seq, a.d_pos, a.Ms, a.Ss,
+                                        a.Mo, a.So, a.prob_bits, a.luts); if (e_ != cudaSuccess) return e_; }
   return cudaGetLastError();
 }
 

@@ -14,6 +14,7 @@
 #include <cstdint>
 
 #include "kernels.h"
+#include "launch.cuh"
 #include "numerics.cuh"
 
 namespace llx {
@@ -51,6 +52,8 @@ __device__ __forceinline__ int dot16(const uint4& w, const uint4& x, int acc) {
 // ---- GEMV: 8 channels per 256-thread block, RB rows per block row ------------------------
 template <int RB>
 __global__ void __launch_bounds__(256) k_gemv(LinearArgs a) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ int32_t part[8][8][RB];  // [warp][channel][row]
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = lane >> 2, sub = lane & 3;
@@ -100,6 +103,8 @@ __global__ void __launch_bounds__(256) k_gemv(LinearArgs a) {
 constexpr int TB = 64, TK = 64, TKW = TK / 4, PADW = TKW + 1;
 
 __global__ void __launch_bounds__(256) k_gemm_tiled(LinearArgs a) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ uint32_t As[TB][PADW];
   __shared__ uint32_t Ws[TB][PADW];
   const int tid = threadIdx.x;
@@ -153,10 +158,10 @@ cudaError_t launch_linear(const LinearArgs& a, int path, cudaStream_t st) {
   if (path == 1) {
     constexpr int RB = 4;
     dim3 grid((a.N + 7) / 8, (a.R + RB - 1) / RB);
-    k_gemv<RB><<<grid, 256, 0, st>>>(a);
+    { const cudaError_t e_ = launch_k(k_gemv<RB>, dim3(grid), dim3(256), 0, st, a); if (e_ != cudaSuccess) return e_; }
   } else {
     dim3 grid((a.N + TB - 1) / TB, (a.R + TB - 1) / TB);
-    k_gemm_tiled<<<grid, 256, 0, st>>>(a);
+    { const cudaError_t e_ = launch_k(k_gemm_tiled, dim3(grid), dim3(256), 0, st, a); if (e_ != cudaSuccess) return e_; }
   }
   return cudaGetLastError();
 }

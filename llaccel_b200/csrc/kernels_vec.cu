@@ -7,9 +7,12 @@
 #include <cstdint>
 
 #include "kernels.h"
+#include "launch.cuh"
 #include "numerics.cuh"
 
 namespace llx {
+
+int g_pdl = 1;
 
 
 static inline unsigned grid1d(int64_t n, int per_block) { return (unsigned)((n + per_block - 1) / per_block); }
@@ -17,6 +20,8 @@ static inline unsigned grid1d(int64_t n, int per_block) { return (unsigned)((n +
 // ---- embedding gather (golden.py:369-373; host.cpp:108-113) ------------------------------
 __global__ void k_embed(const int32_t* __restrict__ tokens, const int16_t* __restrict__ embed,
                         int16_t* __restrict__ out, int R, int dim, int vocab_rows, int32_t* err) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x;
   const int tok = tokens[r];
   const int chunks = dim / 8;
@@ -33,7 +38,7 @@ __global__ void k_embed(const int32_t* __restrict__ tokens, const int16_t* __res
 cudaError_t launch_embed(const int32_t* tokens, const int16_t* embed, int16_t* out, int R, int dim, int vocab_rows,
                          int32_t* err, cudaStream_t st) {
   if (R <= 0) return cudaSuccess;
-  k_embed<<<R, 64, 0, st>>>(tokens, embed, out, R, dim, vocab_rows, err);
+  { const cudaError_t e_ = launch_k(k_embed, dim3(R), dim3(64), 0, st, tokens, embed, out, R, dim, vocab_rows, err); if (e_ != cudaSuccess) return e_; }
   return cudaGetLastError();
 }
 
@@ -66,6 +71,8 @@ __device__ __forceinline__ uint2 pack8_i8(const int32_t* v) {
 __global__ void k_rmsnorm(const int16_t* __restrict__ x, const int16_t* __restrict__ gamma, int16_t* __restrict__ y,
                           int8_t* __restrict__ y8, int nrows, int K, int64_t eps_t, int64_t C, int sh_post,
                           int64_t Mq, int Sq) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= nrows) return;
@@ -111,13 +118,15 @@ cudaError_t launch_rmsnorm(const int16_t* x, const int16_t* gamma, int16_t* y, i
                            int64_t eps_t, int64_t C, int sh_post, int64_t Mq, int Sq, cudaStream_t st) {
   if (nrows <= 0) return cudaSuccess;
   const int warps_per_block = 4;
-  k_rmsnorm<<<grid1d(nrows, warps_per_block), 32 * warps_per_block, 0, st>>>(x, gamma, y, y8, nrows, K, eps_t, C,
-                                                                             sh_post, Mq, Sq);
+  { const cudaError_t e_ = launch_k(k_rmsnorm, dim3(grid1d(nrows, warps_per_block)), dim3(32 * warps_per_block), 0, st, x, gamma, y, y8, nrows, K, eps_t, C,
+                                                                             sh_post, Mq, Sq); if (e_ != cudaSuccess) return e_; }
   return cudaGetLastError();
 }
 
 // ---- QUANT i16 -> i8 (numerics.h:56) -------------------------------------------------------
 __global__ void k_quant(const int16_t* __restrict__ x, int8_t* __restrict__ y, int64_t n8, int64_t M, int S) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n8) return;
   int32_t v[8], q[8];
@@ -130,7 +139,7 @@ __global__ void k_quant(const int16_t* __restrict__ x, int8_t* __restrict__ y, i
 cudaError_t launch_quant(const int16_t* x, int8_t* y, int64_t n, int64_t M, int S, cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
   const int64_t n8 = n / 8;
-  k_quant<<<grid1d(n8, 256), 256, 0, st>>>(x, y, n8, M, S);
+  { const cudaError_t e_ = launch_k(k_quant, dim3(grid1d(n8, 256)), dim3(256), 0, st, x, y, n8, M, S); if (e_ != cudaSuccess) return e_; }
   return cudaGetLastError();
 }
 
@@ -140,6 +149,8 @@ __global__ void k_rope(const int16_t* __restrict__ x, int16_t* __restrict__ y16,
                        int64_t Mq, int Sq, int8_t* __restrict__ kcache, int R, int M, int H, int D,
                        const int16_t* __restrict__ cos_tab, const int16_t* __restrict__ sin_tab,
                        const int* __restrict__ d_pos, int max_seq) {
+  pdl_trigger();
+  pdl_wait();
   const int half = D >> 1;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t total = (int64_t)R * H * half;
@@ -174,8 +185,8 @@ cudaError_t launch_rope(const int16_t* x, int16_t* y16, int8_t* y8, int64_t Mq, 
                         cudaStream_t st) {
   const int64_t total = (int64_t)R * H * (D / 2);
   if (total <= 0) return cudaSuccess;
-  k_rope<<<grid1d(total, 256), 256, 0, st>>>(x, y16, y8, Mq, Sq, kcache, R, M, H, D, cos_tab, sin_tab, d_pos,
-                                             max_seq);
+  { const cudaError_t e_ = launch_k(k_rope, dim3(grid1d(total, 256)), dim3(256), 0, st, x, y16, y8, Mq, Sq, kcache, R, M, H, D, cos_tab, sin_tab, d_pos,
+                                             max_seq); if (e_ != cudaSuccess) return e_; }
   return cudaGetLastError();
 }
 
@@ -184,6 +195,8 @@ cudaError_t launch_rope(const int16_t* x, int16_t* y16, int8_t* y8, int64_t Mq, 
 __global__ void k_kv_write(const int8_t* __restrict__ k, const int8_t* __restrict__ v, int8_t* __restrict__ kc,
                            int8_t* __restrict__ vc, int R, int M, int Hkv, int D, const int* __restrict__ d_pos,
                            int max_seq) {
+  pdl_trigger();
+  pdl_wait();
   const int cpr = D / 16;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t total = (int64_t)R * Hkv * cpr;
@@ -203,13 +216,15 @@ cudaError_t launch_kv_write(const int8_t* k, const int8_t* v, int8_t* kc, int8_t
                             const int* d_pos, int max_seq, cudaStream_t st) {
   const int64_t total = (int64_t)R * Hkv * (D / 16);
   if (total <= 0) return cudaSuccess;
-  k_kv_write<<<grid1d(total, 256), 256, 0, st>>>(k, v, kc, vc, R, M, Hkv, D, d_pos, max_seq);
+  { const cudaError_t e_ = launch_k(k_kv_write, dim3(grid1d(total, 256)), dim3(256), 0, st, k, v, kc, vc, R, M, Hkv, D, d_pos, max_seq); if (e_ != cudaSuccess) return e_; }
   return cudaGetLastError();
 }
 
 // ---- elementwise ADD / MUL / SILU (numerics.h:45-55) ----------------------------------------
 __global__ void k_add(const int16_t* __restrict__ a, const int16_t* __restrict__ b, int16_t* __restrict__ y,
                       int64_t n8, int sh_b) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n8) return;
   int32_t va[8], vb[8], o[8];
@@ -222,6 +237,8 @@ __global__ void k_add(const int16_t* __restrict__ a, const int16_t* __restrict__
 
 __global__ void k_mul(const int16_t* __restrict__ a, const int16_t* __restrict__ b, int16_t* __restrict__ y,
                       int64_t n8, int sh) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n8) return;
   int32_t va[8], vb[8], o[8];
@@ -234,6 +251,8 @@ __global__ void k_mul(const int16_t* __restrict__ a, const int16_t* __restrict__
 
 __global__ void k_silu(const int16_t* __restrict__ x, int16_t* __restrict__ y, int64_t n8, int64_t Mi, int Si,
                        int sh_out, const uint16_t* __restrict__ sig) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n8) return;
   int32_t v[8], o[8];
@@ -245,23 +264,25 @@ __global__ void k_silu(const int16_t* __restrict__ x, int16_t* __restrict__ y, i
 
 cudaError_t launch_add(const int16_t* a, const int16_t* b, int16_t* y, int64_t n, int sh_b, cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
-  k_add<<<grid1d(n / 8, 256), 256, 0, st>>>(a, b, y, n / 8, sh_b);
+  { const cudaError_t e_ = launch_k(k_add, dim3(grid1d(n / 8, 256)), dim3(256), 0, st, a, b, y, n / 8, sh_b); if (e_ != cudaSuccess) return e_; }
   return cudaGetLastError();
 }
 cudaError_t launch_mul(const int16_t* a, const int16_t* b, int16_t* y, int64_t n, int sh, cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
-  k_mul<<<grid1d(n / 8, 256), 256, 0, st>>>(a, b, y, n / 8, sh);
+  { const cudaError_t e_ = launch_k(k_mul, dim3(grid1d(n / 8, 256)), dim3(256), 0, st, a, b, y, n / 8, sh); if (e_ != cudaSuccess) return e_; }
   return cudaGetLastError();
 }
 cudaError_t launch_silu(const int16_t* x, int16_t* y, int64_t n, int64_t Mi, int Si, int sh_out,
                         const uint16_t* luts, cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
-  k_silu<<<grid1d(n / 8, 256), 256, 0, st>>>(x, y, n / 8, Mi, Si, sh_out, luts + kLutSig);
+  { const cudaError_t e_ = launch_k(k_silu, dim3(grid1d(n / 8, 256)), dim3(256), 0, st, x, y, n / 8, Mi, Si, sh_out, luts + kLutSig); if (e_ != cudaSuccess) return e_; }
   return cudaGetLastError();
 }
 
 // ---- argmax over the first `vocab` logits, lowest index on ties (NUMERICS.md:207-208) --------
 __global__ void k_argmax(const int16_t* __restrict__ logits, int ld, int vocab, int32_t* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x;
   const int16_t* row = logits + (int64_t)r * ld;
   // key: value in the high half, inverted index in the low half -> max key = first max
@@ -294,13 +315,15 @@ __global__ void k_argmax(const int16_t* __restrict__ logits, int ld, int vocab, 
 
 cudaError_t launch_argmax(const int16_t* logits, int R, int ld, int vocab, int32_t* out, cudaStream_t st) {
   if (R <= 0) return cudaSuccess;
-  k_argmax<<<R, 512, 0, st>>>(logits, ld, vocab, out);
+  { const cudaError_t e_ = launch_k(k_argmax, dim3(R), dim3(512), 0, st, logits, ld, vocab, out); if (e_ != cudaSuccess) return e_; }
   return cudaGetLastError();
 }
 
 // ---- row gather ----------------------------------------------------------------------------
 __global__ void k_gather_rows(const uint4* __restrict__ src, uint4* __restrict__ dst, const int32_t* __restrict__ idx,
                               int chunks) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x;
   const int64_t s = (int64_t)idx[i] * chunks, d = (int64_t)i * chunks;
   for (int c = threadIdx.x; c < chunks; c += blockDim.x) dst[d + c] = src[s + c];
@@ -309,8 +332,8 @@ __global__ void k_gather_rows(const uint4* __restrict__ src, uint4* __restrict__
 cudaError_t launch_gather_rows(const void* src, void* dst, const int32_t* idx, int n, int row_bytes,
                                cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
-  k_gather_rows<<<n, 128, 0, st>>>(reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), idx,
-                                   row_bytes / 16);
+  { const cudaError_t e_ = launch_k(k_gather_rows, dim3(n), dim3(128), 0, st, reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), idx,
+                                   row_bytes / 16); if (e_ != cudaSuccess) return e_; }
   return cudaGetLastError();
 }
 

@@ -1,0 +1,39 @@
+// Kernel launch helper with programmatic dependent launch (PDL).
+//
+// Every kernel of the datapath calls pdl_trigger() early (its dependents may start
+// launching once every CTA of this grid has triggered or exited) and pdl_wait() before it
+// touches memory that an earlier kernel of the stream writes or reads (griddepcontrol.wait
+// returns once the preceding grid has completed and its writes are visible).  Work that
+// only reads model constants -- weight TMA loads, requant tables, LUTs -- runs before the
+// wait and overlaps the previous kernel.  Launched without the PDL attribute both calls
+// are no-ops, so the same kernels serve either mode.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <utility>
+
+namespace llx {
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// process-wide switch, set from llx_opts at model load (1 = launch with PDL)
+extern int g_pdl;
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = g_pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+}  // namespace llx

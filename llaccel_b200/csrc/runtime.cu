@@ -30,6 +30,7 @@
 #include "../../include/llx.h"
 #include "json.hpp"
 #include "kernels.h"
+#include "launch.cuh"
 #include "luts_data.h"
 #include "numerics.cuh"
 
@@ -869,6 +870,8 @@ static void plan_arena(llx_session* s) {
 
 __global__ void k_decode_finalize(const int32_t* __restrict__ argmax, int32_t* __restrict__ tokens,
                                   int32_t* __restrict__ hist, int32_t* pos, int32_t* step, int B, int cap) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ int s_step;
   if (threadIdx.x == 0) s_step = *step;
   __syncthreads();
@@ -1001,9 +1004,8 @@ static void build_decode_graph(llx_session* s) {
     cudaError_t e = launch_argmax((const int16_t*)bd.p[m->output_act], s->B, m->vocab_padded, m->vocab, s->d_argmax,
                                   s->st);
     if (e != cudaSuccess) throw Error(LLX_ERR_CUDA, cudaGetErrorString(e));
-    k_decode_finalize<<<1, 256, 0, s->st>>>(s->d_argmax, s->d_tokens, s->d_hist, s->d_pos, s->d_step, s->B,
-                                            s->hist_cap);
-    LLX_CUDA(cudaGetLastError());
+    LLX_CUDA(launch_k(k_decode_finalize, dim3(1), dim3(256), 0, s->st, (const int32_t*)s->d_argmax, s->d_tokens,
+                      s->d_hist, s->d_pos, s->d_step, s->B, s->hist_cap));
   } catch (...) {
     cudaStreamEndCapture(s->st, &graph);
     throw;
@@ -1113,7 +1115,9 @@ llx_status llx_model_load(const char* dir, const llx_opts* opts, llx_model** out
     m->opts.device = 0;
     m->opts.fuse = 1;
     m->opts.gemm_path = 0;
+    m->opts.pdl = 1;
     if (opts) m->opts = *opts;
+    g_pdl = m->opts.pdl;
     m->device = m->opts.device;
     int ndev = 0;
     LLX_CUDA(cudaGetDeviceCount(&ndev));

@@ -60,7 +60,7 @@ SIGNATURES = {
 
 
 class LlxOpts(C.Structure):
-    _fields_ = [("device", C.c_int), ("fuse", C.c_int), ("gemm_path", C.c_int)]
+    _fields_ = [("device", C.c_int), ("fuse", C.c_int), ("gemm_path", C.c_int), ("pdl", C.c_int)]
 
 
 class LlxModelInfo(C.Structure):
@@ -119,11 +119,11 @@ class CudaModel:
     activation of the last launch readable (needed for `acts=`)."""
 
     def __init__(self, qgraph_dir, *, batch: int = 1, device: int = 0, max_rows: int | None = None,
-                 keep_acts: bool = False, fuse: bool = True, gemm_path: int = 0) -> None:
+                 keep_acts: bool = False, fuse: bool = True, gemm_path: int = 0, pdl: bool = True) -> None:
         self.lib = load_library()
         self.dir = Path(qgraph_dir)
         self.batch = int(batch)
-        opts = LlxOpts(int(device), 1 if fuse else 0, int(gemm_path))
+        opts = LlxOpts(int(device), 1 if fuse else 0, int(gemm_path), 1 if pdl else 0)
         self._model = C.c_void_p()
         _check(self.lib, self.lib.llx_model_load(str(self.dir).encode(), C.byref(opts), C.byref(self._model)))
         info = LlxModelInfo()
