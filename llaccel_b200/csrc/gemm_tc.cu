@@ -162,6 +162,54 @@ __device__ __forceinline__ int32_t silu_fast(int32_t x, uint32_t Mi, int Si, int
   return sat16_32(rshr_small(x * sg, sh_out));
 }
 
+__device__ __forceinline__ void store16_i16(int16_t* p, const int32_t* o, int cnt) {
+  if (cnt == 16) {
+    uint4 w0, w1;
+    w0.x = (uint32_t)(uint16_t)o[0] | (uint32_t)(uint16_t)o[1] << 16;
+    w0.y = (uint32_t)(uint16_t)o[2] | (uint32_t)(uint16_t)o[3] << 16;
+    w0.z = (uint32_t)(uint16_t)o[4] | (uint32_t)(uint16_t)o[5] << 16;
+    w0.w = (uint32_t)(uint16_t)o[6] | (uint32_t)(uint16_t)o[7] << 16;
+    w1.x = (uint32_t)(uint16_t)o[8] | (uint32_t)(uint16_t)o[9] << 16;
+    w1.y = (uint32_t)(uint16_t)o[10] | (uint32_t)(uint16_t)o[11] << 16;
+    w1.z = (uint32_t)(uint16_t)o[12] | (uint32_t)(uint16_t)o[13] << 16;
+    w1.w = (uint32_t)(uint16_t)o[14] | (uint32_t)(uint16_t)o[15] << 16;
+    reinterpret_cast<uint4*>(p)[0] = w0;
+    reinterpret_cast<uint4*>(p)[1] = w1;
+  } else {
+    for (int j = 0; j < cnt; ++j) p[j] = (int16_t)o[j];
+  }
+}
+__device__ __forceinline__ void store16_i8(int8_t* p, const int32_t* o, int cnt) {
+  if (cnt == 16) {
+    uint4 w;
+    w.x = (uint32_t)(uint8_t)o[0] | (uint32_t)(uint8_t)o[1] << 8 | (uint32_t)(uint8_t)o[2] << 16 |
+          (uint32_t)(uint8_t)o[3] << 24;
+    w.y = (uint32_t)(uint8_t)o[4] | (uint32_t)(uint8_t)o[5] << 8 | (uint32_t)(uint8_t)o[6] << 16 |
+          (uint32_t)(uint8_t)o[7] << 24;
+    w.z = (uint32_t)(uint8_t)o[8] | (uint32_t)(uint8_t)o[9] << 8 | (uint32_t)(uint8_t)o[10] << 16 |
+          (uint32_t)(uint8_t)o[11] << 24;
+    w.w = (uint32_t)(uint8_t)o[12] | (uint32_t)(uint8_t)o[13] << 8 | (uint32_t)(uint8_t)o[14] << 16 |
+          (uint32_t)(uint8_t)o[15] << 24;
+    *reinterpret_cast<uint4*>(p) = w;
+  } else {
+    for (int j = 0; j < cnt; ++j) p[j] = (int8_t)o[j];
+  }
+}
+__device__ __forceinline__ void load16_i16(const int16_t* p, int32_t* v, int cnt) {
+  if (cnt == 16) {
+    const uint4 u0 = reinterpret_cast<const uint4*>(p)[0], u1 = reinterpret_cast<const uint4*>(p)[1];
+    const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      v[2 * j] = (int16_t)(w[j] & 0xFFFF);
+      v[2 * j + 1] = (int16_t)(w[j] >> 16);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = j < cnt ? p[j] : 0;
+  }
+}
+
 template <int NT, int S>
 struct Smem {
   static constexpr int kA = BM * BK;  // 16 KB activation tile
@@ -222,7 +270,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     s_S[i] = n < a.N ? a.rq[2 * n + 1] : 0;
     s_bias[i] = (n < a.N && a.bias) ? (int64_t)a.bias[n] : 0;
   }
-  if (a.epi == EPI_SILU)
+  if (a.epi == EPI_SILU || a.gated)
     for (int i = threadIdx.x; i < 257; i += blockDim.x) s_sig[i] = a.luts[kLutSig + i];
   tc_fence_before();
   __syncthreads();
@@ -329,9 +377,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int r = m0 + row_in_tile;
     const int32_t* part = reinterpret_cast<const int32_t*>(ring);
     const bool narrow = a.narrow != 0;
-#pragma unroll 1
-    for (int c0 = half * 16; c0 < NT; c0 += 32) {
-      int32_t acc[16];
+    // 16 accumulators of channel chunk c0..c0+15 for this thread's row (warp-uniform call)
+    auto fetch = [&](int c0, int32_t* acc) {
       if (ksplit == 1) {
         uint32_t v[16];
         tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + c0, v);
@@ -344,32 +391,65 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
           for (int j = 0; j < 16; ++j) acc[j] += (int32_t)dsmem_ld(part + row_in_tile * NT + c0 + j, p);
       }
-      if (r >= a.R) continue;
-      const int nb = n0 + c0;
-      if (nb >= a.N) continue;
-      const int cnt = min(16, a.N - nb);
-      int32_t o[16];
-      if (a.out_i8) {
+    };
+    if (a.gated) {
+      // chunk pairs (gate, up) -> 16 output channels; pairs alternate between the two warps
+#pragma unroll 1
+      for (int c0 = half * 32; c0 < NT; c0 += 64) {
+        int32_t ag[16], au[16];
+        fetch(c0, ag);
+        fetch(c0 + 16, au);
+        if (r >= a.R) continue;
+        const int ob = (n0 + c0) / 2;  // first output channel of this pair
+        if (ob >= a.Nout) continue;
+        const int cnt = min(16, a.Nout - ob);
+        int32_t sg[16], f[16], fq[16];
+        const uint32_t Mi = (uint32_t)a.silu_Mi;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) o[j] = sat8_64(requant64(acc[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], narrow));
-      } else {
+        for (int j = 0; j < 16; ++j) {
+          const int32_t tg = sat16_64(requant64(ag[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], narrow));
+          const int32_t tu = sat16_64(requant64(au[j], s_bias[c0 + 16 + j], s_M[c0 + 16 + j], s_S[c0 + 16 + j], narrow));
+          sg[j] = silu_fast(tg, Mi, a.silu_Si, a.silu_sh, s_sig);
+          f[j] = sat16_32(rshr_small(tu * sg[j], a.aux_shift));
+          fq[j] = sat8_64(rshr64((int64_t)f[j] * a.q_M, a.q_S));
+        }
+        const int64_t off = (int64_t)r * a.Nout + ob;
+        if (a.g_out) store16_i16(a.g_out + off, sg, cnt);
+        if (a.f_out) store16_i16(a.f_out + off, f, cnt);
+        if (a.q_out) store16_i8(a.q_out + off, fq, cnt);
+      }
+    } else {
+#pragma unroll 1
+      for (int c0 = half * 16; c0 < NT; c0 += 32) {
+        int32_t acc[16];
+        fetch(c0, acc);
+        if (r >= a.R) continue;
+        const int nb = n0 + c0;
+        if (nb >= a.N) continue;
+        // destination: the single output, or the segment holding this chunk
+        void* dst = a.out;
+        int ld = a.N, col = nb, i8 = a.out_i8, cnt = min(16, a.N - nb);
+        if (a.nseg > 0) {
+          int sgi = 0;
+          while (sgi + 1 < a.nseg && nb >= a.seg_start[sgi + 1]) ++sgi;
+          dst = a.seg_out[sgi];
+          ld = a.seg_start[sgi + 1] - a.seg_start[sgi];
+          col = nb - a.seg_start[sgi];
+          i8 = a.seg_i8[sgi];
+          cnt = min(16, a.seg_start[sgi + 1] - nb);
+        }
+        int32_t o[16];
+        if (i8) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] = sat8_64(requant64(acc[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], narrow));
+          store16_i8(reinterpret_cast<int8_t*>(dst) + (int64_t)r * ld + col, o, cnt);
+          continue;
+        }
 #pragma unroll
         for (int j = 0; j < 16; ++j) o[j] = sat16_64(requant64(acc[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], narrow));
         if (a.epi == EPI_RESADD || a.epi == EPI_MUL) {
           int32_t aux[16];
-          const int16_t* ap = a.aux + (int64_t)r * a.N + nb;
-          if (cnt == 16) {
-            const uint4 u0 = reinterpret_cast<const uint4*>(ap)[0], u1 = reinterpret_cast<const uint4*>(ap)[1];
-            const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              aux[2 * j] = (int16_t)(w[j] & 0xFFFF);
-              aux[2 * j + 1] = (int16_t)(w[j] >> 16);
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) aux[j] = j < cnt ? ap[j] : 0;
-          }
+          load16_i16(a.aux + (int64_t)r * a.N + nb, aux, cnt);
           if (a.epi == EPI_RESADD) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) o[j] = sat16_32(o[j] + aux[j]);
@@ -382,40 +462,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
           for (int j = 0; j < 16; ++j) o[j] = silu_fast(o[j], Mi, a.silu_Si, a.silu_sh, s_sig);
         }
-      }
-      if (a.out_i8) {
-        int8_t* op = reinterpret_cast<int8_t*>(a.out) + (int64_t)r * a.N + nb;
-        if (cnt == 16) {
-          uint4 w;
-          w.x = (uint32_t)(uint8_t)o[0] | (uint32_t)(uint8_t)o[1] << 8 | (uint32_t)(uint8_t)o[2] << 16 |
-                (uint32_t)(uint8_t)o[3] << 24;
-          w.y = (uint32_t)(uint8_t)o[4] | (uint32_t)(uint8_t)o[5] << 8 | (uint32_t)(uint8_t)o[6] << 16 |
-                (uint32_t)(uint8_t)o[7] << 24;
-          w.z = (uint32_t)(uint8_t)o[8] | (uint32_t)(uint8_t)o[9] << 8 | (uint32_t)(uint8_t)o[10] << 16 |
-                (uint32_t)(uint8_t)o[11] << 24;
-          w.w = (uint32_t)(uint8_t)o[12] | (uint32_t)(uint8_t)o[13] << 8 | (uint32_t)(uint8_t)o[14] << 16 |
-                (uint32_t)(uint8_t)o[15] << 24;
-          *reinterpret_cast<uint4*>(op) = w;
-        } else {
-          for (int j = 0; j < cnt; ++j) op[j] = (int8_t)o[j];
-        }
-      } else {
-        int16_t* op = reinterpret_cast<int16_t*>(a.out) + (int64_t)r * a.N + nb;
-        if (cnt == 16) {
-          uint4 w0, w1;
-          w0.x = (uint32_t)(uint16_t)o[0] | (uint32_t)(uint16_t)o[1] << 16;
-          w0.y = (uint32_t)(uint16_t)o[2] | (uint32_t)(uint16_t)o[3] << 16;
-          w0.z = (uint32_t)(uint16_t)o[4] | (uint32_t)(uint16_t)o[5] << 16;
-          w0.w = (uint32_t)(uint16_t)o[6] | (uint32_t)(uint16_t)o[7] << 16;
-          w1.x = (uint32_t)(uint16_t)o[8] | (uint32_t)(uint16_t)o[9] << 16;
-          w1.y = (uint32_t)(uint16_t)o[10] | (uint32_t)(uint16_t)o[11] << 16;
-          w1.z = (uint32_t)(uint16_t)o[12] | (uint32_t)(uint16_t)o[13] << 16;
-          w1.w = (uint32_t)(uint16_t)o[14] | (uint32_t)(uint16_t)o[15] << 16;
-          reinterpret_cast<uint4*>(op)[0] = w0;
-          reinterpret_cast<uint4*>(op)[1] = w1;
-        } else {
-          for (int j = 0; j < cnt; ++j) op[j] = (int16_t)o[j];
-        }
+        store16_i16(reinterpret_cast<int16_t*>(dst) + (int64_t)r * ld + col, o, cnt);
       }
     }
   }

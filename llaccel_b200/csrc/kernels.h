@@ -28,6 +28,21 @@ cudaError_t launch_rope(const int16_t* x, int16_t* y16, int8_t* y8, int64_t Mq, 
                         int H, int D, const int16_t* cos_tab, const int16_t* sin_tab, const int* d_pos, int max_seq,
                         cudaStream_t st);
 
+// Both RoPEs of a layer in one launch: job q (no cache) and job k (K cache write), each with
+// fused QUANT, plus the V rows copied into vcache.  Row r is at position pos + r % M.
+struct RopeJob {
+  const int16_t* x;
+  int16_t* y16;
+  int8_t* y8;
+  int64_t Mq;
+  int Sq;
+  int8_t* kcache;
+  int H;
+};
+cudaError_t launch_rope_group(const RopeJob& q, const RopeJob& k, const int8_t* v, int8_t* vcache, int Hkv, int R,
+                              int M, int D, const int16_t* cos_tab, const int16_t* sin_tab, const int* d_pos,
+                              int max_seq, cudaStream_t st);
+
 // k, v [R][Hkv*D] i8 -> caches [B][Hkv][max_seq][D] at positions pos + m
 cudaError_t launch_kv_write(const int8_t* k, const int8_t* v, int8_t* kc, int8_t* vc, int R, int M, int Hkv, int D,
                             const int* d_pos, int max_seq, cudaStream_t st);
@@ -63,6 +78,23 @@ struct LinearArgs {
   int aux_shift;
   const uint16_t* luts;  // device tables (SILU epilogue)
   int narrow;            // 1: |acc + bias| < 2^31 for every channel (proved at load), 32-bit bias add
+  // Fused multi-output linear (several linears sharing A, epilogue none): channel segments
+  // [seg_start[i], seg_start[i+1]) of the concatenated W go to seg_out[i] (row stride =
+  // segment width, i8 when seg_i8[i]).  nseg = 0: single output `out`.
+  int nseg;
+  int seg_start[5];
+  void* seg_out[4];
+  int seg_i8[4];
+  // Fused gate/up pair: W rows interleave 16 gate rows and 16 up rows; channel block j of
+  // 16 outputs is gate chunk 2j and up chunk 2j+1.  Per output channel:
+  //   sg = silu16(requant16(acc_g)); f = sat16(rshr(requant16(acc_u) * sg, aux_shift));
+  //   fq = sat8(mulshift(f, q_M, q_S)).  Outputs [R][Nout]; each may be null.
+  int gated, Nout;
+  int16_t* g_out;
+  int16_t* f_out;
+  int8_t* q_out;
+  int64_t q_M;
+  int q_S;
 };
 
 // CUDA-core paths: 0 = auto, 1 = GEMV (small R), 2 = tiled dp4a

@@ -4,6 +4,7 @@
 // this path is a multiple of 16 elements, NUMERICS.md "Counts are multiples of 16").
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 
 #include "kernels.h"
@@ -187,6 +188,72 @@ cudaError_t launch_rope(const int16_t* x, int16_t* y16, int8_t* y8, int64_t Mq, 
   if (total <= 0) return cudaSuccess;
   { const cudaError_t e_ = launch_k(k_rope, dim3(grid1d(total, 256)), dim3(256), 0, st, x, y16, y8, Mq, Sq, kcache, R, M, H, D, cos_tab, sin_tab, d_pos,
                                              max_seq); if (e_ != cudaSuccess) return e_; }
+  return cudaGetLastError();
+}
+
+// ---- RoPE group: q and k rotations (+ QUANT, K cache) and the V cache copy, one launch --------
+__device__ __forceinline__ void rope_pair(const RopeJob& j, int r, int h, int i, int M, int D, int p,
+                                          const int16_t* __restrict__ cos_tab, const int16_t* __restrict__ sin_tab,
+                                          int max_seq) {
+  const int half = D >> 1;
+  const int64_t base = (int64_t)r * j.H * D + (int64_t)h * D;
+  const int64_t x1 = j.x[base + i], x2 = j.x[base + i + half];
+  const int64_t c = cos_tab[(int64_t)p * half + i], s = sin_tab[(int64_t)p * half + i];
+  const int64_t a = sat16(rshr(x1 * c - x2 * s, 14));
+  const int64_t b = sat16(rshr(x2 * c + x1 * s, 14));
+  j.y16[base + i] = (int16_t)a;
+  j.y16[base + i + half] = (int16_t)b;
+  if (j.y8) {
+    const int8_t qa = (int8_t)sat8(mulshift(a, j.Mq, j.Sq)), qb = (int8_t)sat8(mulshift(b, j.Mq, j.Sq));
+    j.y8[base + i] = qa;
+    j.y8[base + i + half] = qb;
+    if (j.kcache) {
+      int8_t* dst = j.kcache + (((int64_t)(r / M) * j.H + h) * max_seq + p) * D;
+      dst[i] = qa;
+      dst[i + half] = qb;
+    }
+  }
+}
+
+__global__ void k_rope_group(RopeJob q, RopeJob k, const int8_t* __restrict__ v, int8_t* __restrict__ vcache,
+                             int Hkv, int R, int M, int D, const int16_t* __restrict__ cos_tab,
+                             const int16_t* __restrict__ sin_tab, const int* __restrict__ d_pos, int max_seq) {
+  pdl_trigger();
+  pdl_wait();
+  const int half = D >> 1;
+  const int64_t nq = (int64_t)R * q.H * half, nk = (int64_t)R * k.H * half;
+  const int cpr = D / 16;
+  const int64_t nv = v ? (int64_t)R * Hkv * cpr : 0;
+  const int pos = *d_pos;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < nq + nk + nv;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    if (idx < nq + nk) {
+      const RopeJob& j = idx < nq ? q : k;
+      const int64_t t = idx < nq ? idx : idx - nq;
+      const int i = (int)(t % half);
+      const int h = (int)((t / half) % j.H);
+      const int r = (int)(t / ((int64_t)half * j.H));
+      rope_pair(j, r, h, i, M, D, pos + r % M, cos_tab, sin_tab, max_seq);
+    } else {
+      const int64_t t = idx - nq - nk;
+      const int c = (int)(t % cpr);
+      const int h = (int)((t / cpr) % Hkv);
+      const int r = (int)(t / ((int64_t)cpr * Hkv));
+      const int64_t src = (int64_t)r * Hkv * D + (int64_t)h * D + c * 16;
+      const int64_t dst = (((int64_t)(r / M) * Hkv + h) * max_seq + pos + r % M) * D + c * 16;
+      *reinterpret_cast<uint4*>(vcache + dst) = *reinterpret_cast<const uint4*>(v + src);
+    }
+  }
+}
+
+cudaError_t launch_rope_group(const RopeJob& q, const RopeJob& k, const int8_t* v, int8_t* vcache, int Hkv, int R,
+                              int M, int D, const int16_t* cos_tab, const int16_t* sin_tab, const int* d_pos,
+                              int max_seq, cudaStream_t st) {
+  const int64_t total = (int64_t)R * (q.H + k.H) * (D / 2) + (v ? (int64_t)R * Hkv * (D / 16) : 0);
+  if (total <= 0) return cudaSuccess;
+  const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 16);
+  { const cudaError_t e_ = launch_k(k_rope_group, dim3((unsigned)blocks), dim3(256), 0, st, q, k, v, vcache, Hkv, R, M, D,
+                                    cos_tab, sin_tab, d_pos, max_seq); if (e_ != cudaSuccess) return e_; }
   return cudaGetLastError();
 }
 

@@ -72,7 +72,7 @@ struct ActInfo {
   int elem = 2;
 };
 
-enum class SK { Embed, RmsNorm, Quant, Linear, Rope, KvWrite, Attention, Add, Mul, Silu };
+enum class SK { Embed, RmsNorm, Quant, Linear, Rope, KvWrite, Attention, Add, Mul, Silu, LinearGroup, Gated, RopeGroup };
 
 struct Step {
   SK kind;
@@ -91,7 +91,45 @@ struct Step {
   int Ss = 0, So = 0, prob_bits = 8;
   int sh = 0;
   std::string label;
+  // fused steps: the constituent steps (executed one by one when the fused kernel does not
+  // apply, e.g. on the CUDA-core GEMM path) and the concatenated / interleaved weights
+  std::vector<Step> parts;
+  int nseg = 0;
+  int seg_start[5] = {0, 0, 0, 0, 0};
 };
+
+static std::vector<int> step_outs(const Step& x) {
+  std::vector<int> v;
+  if (!x.parts.empty()) {
+    for (const Step& p : x.parts)
+      for (int a : step_outs(p)) v.push_back(a);
+    return v;
+  }
+  for (int a : {x.out, x.out2})
+    if (a >= 0) v.push_back(a);
+  return v;
+}
+
+static std::vector<int> step_ins(const Step& x) {
+  std::vector<int> v;
+  if (!x.parts.empty()) {
+    std::vector<int> made;
+    for (const Step& p : x.parts) {
+      for (int a : step_ins(p))
+        if (std::find(made.begin(), made.end(), a) == made.end()) v.push_back(a);
+      for (int a : step_outs(p)) made.push_back(a);
+    }
+    return v;
+  }
+  for (int a : {x.in, x.in2})
+    if (a >= 0) v.push_back(a);
+  return v;
+}
+
+static bool writes_kv(const Step& x) {
+  if (x.kind == SK::Attention || x.kind == SK::KvWrite || x.kind == SK::RopeGroup) return true;
+  return x.kind == SK::Rope && x.write_k;
+}
 
 struct LayerKV {
   int Hkv = 0, D = 0;
@@ -238,7 +276,149 @@ static void check_rq_table(const std::vector<uint8_t>& blob, const TensorSpec& t
   }
 }
 
-static void build_plan(llx_model* m, const json::Value& g, const std::vector<uint8_t>& blob) {
+static int64_t append_blob(std::vector<uint8_t>& blob, const void* src, size_t n) {
+  const size_t off = (blob.size() + 63) & ~size_t(63);
+  blob.resize(off + n);
+  std::memcpy(blob.data() + off, src, n);
+  return (int64_t)off;
+}
+
+// Multi-output GEMM over the row-concatenation of the parts' weights (same input, epilogue
+// none).  Segment boundaries stay 16-channel aligned so no epilogue chunk straddles two.
+static bool make_linear_group(std::vector<uint8_t>& blob, const std::vector<Step>& parts, Step* out) {
+  if (parts.size() < 2 || parts.size() > 4) return false;
+  const int K = parts[0].K;
+  int N = 0;
+  bool any_bias = false;
+  for (const Step& p : parts) {
+    if (p.kind != SK::Linear || p.epi != EPI_NONE || p.K != K || p.in != parts[0].in || p.N % 16) return false;
+    N += p.N;
+    any_bias |= p.bias_off >= 0;
+  }
+  std::vector<int8_t> w((size_t)N * K);
+  std::vector<int32_t> rq((size_t)N * 2), bias((size_t)N, 0);
+  Step g;
+  g.kind = SK::LinearGroup;
+  g.in = parts[0].in;
+  g.K = K;
+  g.N = N;
+  g.nseg = (int)parts.size();
+  int n0 = 0;
+  int64_t max_bias = 0;
+  for (size_t i = 0; i < parts.size(); ++i) {
+    const Step& p = parts[i];
+    g.seg_start[i] = n0;
+    std::memcpy(w.data() + (size_t)n0 * K, blob.data() + p.w_off, (size_t)p.N * K);
+    std::memcpy(rq.data() + (size_t)n0 * 2, blob.data() + p.rq_off, (size_t)p.N * 8);
+    if (p.bias_off >= 0) {
+      std::memcpy(bias.data() + n0, blob.data() + p.bias_off, (size_t)p.N * 4);
+      for (int j = 0; j < p.N; ++j) max_bias = std::max<int64_t>(max_bias, std::llabs((long long)bias[n0 + j]));
+    }
+    n0 += p.N;
+  }
+  g.seg_start[parts.size()] = N;
+  g.narrow = (int64_t)K * 16384 + max_bias < (1ll << 31) ? 1 : 0;
+  g.w_off = append_blob(blob, w.data(), w.size());
+  g.rq_off = append_blob(blob, rq.data(), rq.size() * 4);
+  g.bias_off = any_bias ? append_blob(blob, bias.data(), bias.size() * 4) : -1;
+  g.parts = parts;
+  g.label = "linear_group:" + parts[0].label;
+  *out = g;
+  return true;
+}
+
+// Gate/up pair (+ the quant of their product): weights, requant pairs and biases
+// interleaved in 16-row blocks (gate block j, up block j), one GEMM of 2N channels.
+static bool make_gated(std::vector<uint8_t>& blob, const std::vector<Step>& parts, Step* out) {
+  const Step& gs = parts[0];
+  const Step& us = parts[1];
+  if (gs.N % 16 || gs.N != us.N || gs.K != us.K) return false;
+  const int N = gs.N, K = gs.K;
+  std::vector<int8_t> w((size_t)2 * N * K);
+  std::vector<int32_t> rq((size_t)4 * N), bias((size_t)2 * N, 0);
+  const bool any_bias = gs.bias_off >= 0 || us.bias_off >= 0;
+  int64_t max_bias = 0;
+  for (int blk = 0; blk < N / 16; ++blk) {
+    for (int h = 0; h < 2; ++h) {
+      const Step& p = h ? us : gs;
+      const size_t dst_row = (size_t)blk * 32 + h * 16, src_row = (size_t)blk * 16;
+      std::memcpy(w.data() + dst_row * K, blob.data() + p.w_off + src_row * K, (size_t)16 * K);
+      std::memcpy(rq.data() + dst_row * 2, blob.data() + p.rq_off + src_row * 8, 16 * 8);
+      if (p.bias_off >= 0) {
+        std::memcpy(bias.data() + dst_row, blob.data() + p.bias_off + src_row * 4, 16 * 4);
+        for (int j = 0; j < 16; ++j) max_bias = std::max<int64_t>(max_bias, std::llabs((long long)bias[dst_row + j]));
+      }
+    }
+  }
+  Step g;
+  g.kind = SK::Gated;
+  g.in = gs.in;
+  g.K = K;
+  g.N = 2 * N;
+  g.narrow = (int64_t)K * 16384 + max_bias < (1ll << 31) ? 1 : 0;
+  g.w_off = append_blob(blob, w.data(), w.size());
+  g.rq_off = append_blob(blob, rq.data(), rq.size() * 4);
+  g.bias_off = any_bias ? append_blob(blob, bias.data(), bias.size() * 4) : -1;
+  g.parts = parts;
+  g.label = "gated:" + us.label;
+  *out = g;
+  return true;
+}
+
+// Second plan pass: multi-output q/k/v GEMMs, gate/up pairs, and the per-layer RoPE group.
+static void fuse_steps(llx_model* m, std::vector<uint8_t>& blob) {
+  std::vector<Step>& st = m->steps;
+  std::vector<Step> out;
+  size_t i = 0;
+  while (i < st.size()) {
+    const Step& x = st[i];
+    if (x.kind == SK::Linear && x.epi == EPI_NONE) {
+      size_t j = i + 1;
+      while (j < st.size() && st[j].kind == SK::Linear && st[j].epi == EPI_NONE && st[j].in == x.in && st[j].K == x.K)
+        ++j;
+      Step grp;
+      if (j - i >= 2 && make_linear_group(blob, std::vector<Step>(st.begin() + i, st.begin() + j), &grp)) {
+        out.push_back(grp);
+        i = j;
+        continue;
+      }
+    }
+    if (x.kind == SK::Linear && x.epi == EPI_SILU && !x.out_i8 && i + 1 < st.size()) {
+      const Step& u = st[i + 1];
+      if (u.kind == SK::Linear && u.epi == EPI_MUL && u.in == x.in && u.in2 == x.out && !u.out_i8) {
+        std::vector<Step> parts{x, u};
+        if (i + 2 < st.size() && st[i + 2].kind == SK::Quant && st[i + 2].in == u.out) parts.push_back(st[i + 2]);
+        Step grp;
+        if (make_gated(blob, parts, &grp)) {
+          out.push_back(grp);
+          i += parts.size();
+          continue;
+        }
+      }
+    }
+    if (x.kind == SK::Rope && !x.write_k && x.out2 >= 0 && i + 2 < st.size()) {
+      const Step& k = st[i + 1];
+      const Step& v = st[i + 2];
+      if (k.kind == SK::Rope && k.write_k && k.out2 >= 0 && k.D == x.D && v.kind == SK::KvWrite && v.in < 0 &&
+          v.layer == k.layer && v.Hkv == k.H && v.D == k.D) {
+        Step grp;
+        grp.kind = SK::RopeGroup;
+        grp.parts = {x, k, v};
+        grp.layer = k.layer;
+        grp.D = x.D;
+        grp.label = "rope_group:" + x.label;
+        out.push_back(grp);
+        i += 3;
+        continue;
+      }
+    }
+    out.push_back(x);
+    ++i;
+  }
+  st.swap(out);
+}
+
+static void build_plan(llx_model* m, const json::Value& g, std::vector<uint8_t>& blob) {
   const json::Value& ops = g.at("ops");
   require(ops.kind == json::Value::Array, LLX_ERR_INVALID, "qgraph 'ops' is not a list");
   m->n_ops = (int)ops.arr.size();
@@ -467,6 +647,7 @@ static void build_plan(llx_model* m, const json::Value& g, const std::vector<uin
     step_of_op[i] = m->steps.size();
     m->steps.push_back(s);
   }
+  if (fuse) fuse_steps(m, blob);
   auto it = m->act_id.find(out_name);
   require(it != m->act_id.end(), LLX_ERR_INVALID, "qgraph output '" + out_name + "' is never produced");
   m->output_act = it->second;
@@ -475,18 +656,16 @@ static void build_plan(llx_model* m, const json::Value& g, const std::vector<uin
   // row-independent tail: everything after the last attention / KV write
   int last = 0;
   for (size_t i = 0; i < m->steps.size(); ++i)
-    if (m->steps[i].kind == SK::Attention || m->steps[i].kind == SK::KvWrite ||
-        (m->steps[i].kind == SK::Rope && m->steps[i].write_k))
-      last = (int)i;
+    if (writes_kv(m->steps[i])) last = (int)i;
   m->tail_start = last + 1;
   std::vector<char> seen(m->acts.size(), 0);
   for (size_t i = m->tail_start; i < m->steps.size(); ++i) {
-    const Step& s = m->steps[i];
-    for (int a : {s.in, s.in2}) {
-      if (a < 0 || seen[a]) continue;
+    for (int a : step_ins(m->steps[i])) {
+      if (seen[a]) continue;
       bool defined_in_tail = false;
       for (size_t j = m->tail_start; j < i; ++j)
-        if (m->steps[j].out == a || m->steps[j].out2 == a) defined_in_tail = true;
+        for (int o : step_outs(m->steps[j]))
+          if (o == a) defined_in_tail = true;
       if (!defined_in_tail) {
         seen[a] = 1;
         m->tail_inputs.push_back(a);
@@ -671,13 +850,26 @@ static void pick_tc_tiling(int R, int N, int K, int sms, int* nt, int* ksplit) {
 }
 
 // Enqueue steps [from, to) over R rows (M rows per sequence).
+static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, int M);
+
 static int enqueue_steps(llx_session* s, const Binding& bd, size_t from, size_t to, int R, int M) {
+  int launches = 0;
+  for (size_t i = from; i < to; ++i) launches += enqueue_one(s, bd, s->m->steps[i], R, M);
+  return launches;
+}
+
+// GEMM path of a linear step over R rows: 3 = tensor cores, else a CUDA-core schedule
+static int gemm_path_for(const llx_model* m, int R) {
+  int path = m->opts.gemm_path;
+  if (path == 0) path = R >= 16 ? 3 : 1;
+  return path;
+}
+
+static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, int M) {
   llx_model* m = s->m;
   cudaStream_t st = s->st;
-  int launches = 0;
   auto P = [&](int a) { return a < 0 ? nullptr : bd.p[a]; };
-  for (size_t i = from; i < to; ++i) {
-    const Step& x = m->steps[i];
+  {
     cudaError_t e = cudaSuccess;
     switch (x.kind) {
       case SK::Embed:
@@ -710,8 +902,7 @@ static int enqueue_steps(llx_session* s, const Binding& bd, size_t from, size_t 
         a.aux_shift = x.aux_shift;
         a.luts = m->d_luts;
         a.narrow = x.narrow;
-        int path = m->opts.gemm_path;
-        if (path == 0) path = R >= 16 ? 3 : 1;
+        const int path = gemm_path_for(m, R);
         if (path == 3) {
           int nt = 16, ks = 1;
           pick_tc_tiling(R, x.N, x.K, m->sms, &nt, &ks);
@@ -759,6 +950,71 @@ static int enqueue_steps(llx_session* s, const Binding& bd, size_t from, size_t 
         e = launch_attention(a, st);
         break;
       }
+      case SK::LinearGroup:
+      case SK::Gated: {
+        if (gemm_path_for(m, R) != 3) {
+          // CUDA-core schedules run the constituent ops one by one
+          int n = 0;
+          for (const Step& p : x.parts) n += enqueue_one(s, bd, p, R, M);
+          return n;
+        }
+        LinearArgs a{};
+        a.A = (const int8_t*)P(x.in);
+        a.W = (const int8_t*)dptr(m, x.w_off);
+        a.bias = (const int32_t*)dptr(m, x.bias_off);
+        a.rq = (const int32_t*)dptr(m, x.rq_off);
+        a.R = R;
+        a.N = x.N;
+        a.K = x.K;
+        a.luts = m->d_luts;
+        a.narrow = x.narrow;
+        if (x.kind == SK::LinearGroup) {
+          a.nseg = x.nseg;
+          for (int i = 0; i <= x.nseg; ++i) a.seg_start[i] = x.seg_start[i];
+          for (int i = 0; i < x.nseg; ++i) {
+            a.seg_out[i] = P(x.parts[i].out);
+            a.seg_i8[i] = x.parts[i].out_i8;
+          }
+        } else {
+          const Step& g = x.parts[0];
+          const Step& u = x.parts[1];
+          a.gated = 1;
+          a.Nout = u.N;
+          a.silu_Mi = g.silu_Mi;
+          a.silu_Si = g.silu_Si;
+          a.silu_sh = g.silu_sh;
+          a.aux_shift = u.aux_shift;
+          a.g_out = (int16_t*)P(g.out);
+          a.f_out = (int16_t*)P(u.out);
+          if (x.parts.size() > 2) {
+            a.q_out = (int8_t*)P(x.parts[2].out);
+            a.q_M = x.parts[2].Mq;
+            a.q_S = x.parts[2].Sq;
+          }
+        }
+        int nt = 16, ks = 1;
+        pick_tc_tiling(R, x.N, x.K, m->sms, &nt, &ks);
+        if (x.kind == SK::Gated && nt < 32) {
+          nt = 32;
+          ks = 1;
+        }
+        const CUtensorMap& ma = tmap(s, a.A, (int64_t)bd.rows[x.in], x.K, 128);
+        const CUtensorMap& mw = tmap(s, a.W, x.N, x.K, nt);
+        e = launch_linear_tc(ma, mw, a, nt, ks, s->d_fault, st);
+        break;
+      }
+      case SK::RopeGroup: {
+        const Step& q = x.parts[0];
+        const Step& k = x.parts[1];
+        const Step& v = x.parts[2];
+        auto kv = s->kv_layer.at(k.layer);
+        RopeJob jq{(const int16_t*)P(q.in), (int16_t*)P(q.out), (int8_t*)P(q.out2), q.Mq, q.Sq, nullptr, q.H};
+        RopeJob jk{(const int16_t*)P(k.in), (int16_t*)P(k.out), (int8_t*)P(k.out2), k.Mq, k.Sq, kv.first, k.H};
+        e = launch_rope_group(jq, jk, (const int8_t*)P(v.in2), s->kv_layer.at(v.layer).second, v.Hkv, R, M, q.D,
+                              (const int16_t*)dptr(m, m->cos_off), (const int16_t*)dptr(m, m->sin_off), s->d_pos,
+                              m->max_seq, st);
+        break;
+      }
       case SK::Add:
         e = launch_add((const int16_t*)P(x.in), (const int16_t*)P(x.in2), (int16_t*)P(x.out),
                        (int64_t)R * m->acts[x.in].cols, x.sh, st);
@@ -773,9 +1029,8 @@ static int enqueue_steps(llx_session* s, const Binding& bd, size_t from, size_t 
         break;
     }
     if (e != cudaSuccess) throw Error(LLX_ERR_CUDA, "launch of step '" + x.label + "' failed: " + cudaGetErrorString(e));
-    ++launches;
   }
-  return launches;
+  return 1;
 }
 
 // ---- activation arena: first-fit reuse by liveness over the step list -------------------------
@@ -827,8 +1082,7 @@ static void plan_arena(llx_session* s) {
   const size_t na = m->acts.size();
   std::vector<char> in_tail(na, 0);
   for (size_t i = m->tail_start; i < m->steps.size(); ++i)
-    for (int a : {m->steps[i].out, m->steps[i].out2})
-      if (a >= 0) in_tail[a] = 1;
+    for (int a : step_outs(m->steps[i])) in_tail[a] = 1;
   std::vector<size_t> bytes(na);
   s->act_rows.assign(na, 0);
   s->tail_rows_alloc = tail_rows;
@@ -845,10 +1099,8 @@ static void plan_arena(llx_session* s) {
     std::vector<int> def(na, ns), last(na, -1);
     for (int i = 0; i < ns; ++i) {
       const Step& x = m->steps[i];
-      for (int a : {x.out, x.out2})
-        if (a >= 0) def[a] = std::min(def[a], i);
-      for (int a : {x.in, x.in2})
-        if (a >= 0) last[a] = std::max(last[a], i);
+      for (int a : step_outs(x)) def[a] = std::min(def[a], i);
+      for (int a : step_ins(x)) last[a] = std::max(last[a], i);
     }
     last[m->output_act] = ns;
     for (size_t a = 0; a < na; ++a) last[a] = std::max(last[a], def[a]);
@@ -1432,6 +1684,28 @@ llx_status llx_profile_decode(llx_session* s, int pos, int iters, float* ms, dou
           case SK::Add:
           case SK::Mul: b = 6.0 * R * cols(x.in); break;
           case SK::Silu: b = 4.0 * R * cols(x.in); break;
+          case SK::LinearGroup:
+          case SK::Gated:
+            for (const Step& p : x.parts) {
+              if (p.kind == SK::Linear) {
+                b += (double)p.N * p.K + 8.0 * p.N + (p.bias_off >= 0 ? 4.0 * p.N : 0.0) +
+                     (double)R * p.N * (p.out_i8 ? 1 : 2);
+                o += 2.0 * R * p.N * p.K;
+              } else if (p.kind == SK::Quant) {
+                b += (double)R * cols(p.out);
+              }
+            }
+            if (x.kind == SK::Gated) b -= 2.0 * R * x.parts[0].N;  // the gate output is not re-read
+            b += (double)R * x.K;
+            break;
+          case SK::RopeGroup:
+            for (const Step& p : x.parts) {
+              if (p.kind == SK::Rope)
+                b += R * p.H * p.D * 5.0 + R * 2.0 * p.D + (p.write_k ? 1.0 * R * p.H * p.D : 0.0);
+              else
+                b += 2.0 * R * p.Hkv * p.D;
+            }
+            break;
         }
       } else {
         b = 2.0 * R * m->vocab_padded + 4.0 * R;
@@ -1487,7 +1761,8 @@ llx_status llx_read_activation(llx_session* s, const char* name, void* dst, size
     require(s->keep || a == m->output_act, LLX_ERR_INVALID, "activation buffers are reused; create the session with keep_acts=1");
     bool in_tail = false;
     for (size_t i = m->tail_start; i < m->steps.size(); ++i)
-      if (m->steps[i].out == a || m->steps[i].out2 == a) in_tail = true;
+      for (int o : step_outs(m->steps[i]))
+        if (o == a) in_tail = true;
     const int rows = (s->last_tail && in_tail) ? s->last_Rtail : s->last_R;
     const size_t need = (size_t)rows * m->acts[a].cols * m->acts[a].elem;
     require(bytes >= need, LLX_ERR_INVALID, "destination too small");
