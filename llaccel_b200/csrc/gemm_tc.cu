@@ -126,10 +126,14 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ uint32_t dsmem_ld(const void* local, uint32_t rank) {
-  uint32_t remote, v;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(remote) : "memory");
+// 16 bytes of a cluster peer's shared memory at the address of `local` in this CTA
+__device__ __forceinline__ uint4 dsmem_ld4(const void* local, uint32_t rank) {
+  uint32_t remote;
+  uint4 v;
+  asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(remote));
   return v;
 }
 
@@ -370,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // all threads of every CTA in the cluster meet here (partials visible cluster-wide)
     cluster_sync();
   }
-  if (warp >= 2 && !abort_flag && (ksplit == 1 || crank == 0)) {
+  if (warp >= 2 && !abort_flag) {
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row_in_tile = q * 32 + lane;
@@ -385,17 +389,30 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int j = 0; j < 16; ++j) acc[j] = nkb > 0 ? (int32_t)v[j] : 0;
       } else {
+        // this rank owns chunk c0: sum the partial tiles of every CTA of the cluster
 #pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] = part[row_in_tile * NT + c0 + j];
-        for (uint32_t p = 1; p < (uint32_t)ksplit; ++p)
+        for (int j = 0; j < 16; ++j) acc[j] = 0;
+        const int32_t* src = part + row_in_tile * NT + c0;
+        for (uint32_t p = 0; p < (uint32_t)ksplit; ++p) {
+          uint4 v[4];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) acc[j] += (int32_t)dsmem_ld(part + row_in_tile * NT + c0 + j, p);
+          for (int k = 0; k < 4; ++k) v[k] = dsmem_ld4(src + 4 * k, p);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            acc[4 * k] += (int32_t)v[k].x;
+            acc[4 * k + 1] += (int32_t)v[k].y;
+            acc[4 * k + 2] += (int32_t)v[k].z;
+            acc[4 * k + 3] += (int32_t)v[k].w;
+          }
+        }
       }
     };
     if (a.gated) {
       // chunk pairs (gate, up) -> 16 output channels; pairs alternate between the two warps
 #pragma unroll 1
-      for (int c0 = half * 32; c0 < NT; c0 += 64) {
+      for (int ci = 0; ci < NT / 32; ++ci) {
+        if (ci % ksplit != (int)crank || (ci / ksplit) % 2 != half) continue;
+        const int c0 = ci * 32;
         int32_t ag[16], au[16];
         fetch(c0, ag);
         fetch(c0 + 16, au);
@@ -420,7 +437,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     } else {
 #pragma unroll 1
-      for (int c0 = half * 16; c0 < NT; c0 += 32) {
+      for (int ci = 0; ci < NT / 16; ++ci) {
+        if (ci % ksplit != (int)crank || (ci / ksplit) % 2 != half) continue;
+        const int c0 = ci * 16;
         int32_t acc[16];
         fetch(c0, acc);
         if (r >= a.R) continue;

@@ -826,30 +826,31 @@ static const CUtensorMap& tmap(llx_session* s, const void* base, int64_t rows, i
   return s->tmaps.emplace(key, mp).first->second;
 }
 
-// Tensor-core tiling for R rows x N channels x K: the widest channel tile that still
-// fills the GPU, else the narrowest tile with K split across a cluster.
+// Tensor-core tiling for R rows x N channels x K.  Enough CTAs to cover the SMs, each
+// with at least two 128-byte K blocks; among those, the widest channel tile (the activation
+// tile is re-read once per channel tile) and the smallest cluster split of K.
 static void pick_tc_tiling(int R, int N, int K, int sms, int* nt, int* ksplit) {
   const int row_tiles = (R + 127) / 128;
+  const int nkb = (K + 127) / 128;
   const int cands[5] = {256, 128, 64, 32, 16};
   for (int c : cands) {
-    if ((int64_t)((N + c - 1) / c) * row_tiles >= sms) {
-      *nt = c;
-      *ksplit = 1;
-      return;
+    const int tiles = (N + c - 1) / c * row_tiles;
+    for (int ks = 1; ks <= 8; ks *= 2) {
+      if (ks > 1 && nkb / ks < 2) break;
+      if (tiles * ks >= sms) {
+        *nt = c;
+        *ksplit = ks;
+        return;
+      }
     }
   }
+  // small problem: narrowest tile, deepest split that keeps two K blocks per CTA
   *nt = 16;
-  const int ctas = (N + 15) / 16 * row_tiles;
-  const int nkb = (K + 127) / 128;
-  int ks = (sms + ctas - 1) / ctas;
-  ks = std::min(ks, 8);
-  ks = std::min(ks, std::max(1, nkb / 2));
-  int p2 = 1;
-  while (p2 * 2 <= ks) p2 *= 2;  // cluster sizes 1, 2, 4, 8
-  *ksplit = p2;
+  int ks = 1;
+  while (ks < 8 && nkb / (ks * 2) >= 2) ks *= 2;
+  *ksplit = ks;
 }
 
-// Enqueue steps [from, to) over R rows (M rows per sequence).
 static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, int M);
 
 static int enqueue_steps(llx_session* s, const Binding& bd, size_t from, size_t to, int R, int M) {
