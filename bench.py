@@ -55,6 +55,7 @@ def parse_args():
     ap.add_argument("--cpu-decode", type=int, default=8, help="decode launches in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gemm-path", type=int, default=0)
+    ap.add_argument("--lanes", type=int, default=4, help="concurrent decode lanes (sub-batches on own streams)")
     return ap.parse_args()
 
 
@@ -289,20 +290,21 @@ def run_ours(args, dist: Dist) -> None:
     import torch
     from llaccel_b200 import build
     build.build()
-    from llaccel_b200.cuda_backend import CudaModel
+    from llaccel_b200.cuda_backend import CudaLanes
 
     cfg, w, n_dec = workload(args)
     dev = dist.local
     torch.cuda.set_device(dev)
     qdir = make_artefact(args, dist)
     B, L = w["batch"], w["prompt"]
+    lanes = args.lanes if B % args.lanes == 0 else 1
     prompts = prompts_for(dist.rank, B, L, cfg.vocab)
-    m = CudaModel(qdir, batch=B, device=dev, max_rows=min(L, 512), gemm_path=args.gemm_path)
+    m = CudaLanes(qdir, batch=B, lanes=lanes, device=dev, max_rows=min(L, 512), gemm_path=args.gemm_path)
     t0 = time.perf_counter()
     recs = m.generate_batch(prompts.tolist(), 0, with_logits=False)  # prefill (untimed)
     prefill_s = time.perf_counter() - t0
     first = np.array([r["argmax_per_step"][-1] for r in recs], np.int32)
-    stream = torch.cuda.ExternalStream(m.stream_handle(), device=dev)
+    streams = [torch.cuda.ExternalStream(h, device=dev) for h in m.streams()]
 
     def step():
         m.set_tokens(first)
@@ -317,11 +319,18 @@ def run_ours(args, dist: Dist) -> None:
     torch.cuda.synchronize(dev)
     clocks.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    # set_tokens synchronises the session stream; decode launches are asynchronous
-    e0.record(stream)
+    ends = [torch.cuda.Event() for _ in streams]
+    # every lane stream starts after e0; e1 follows the last lane; set_tokens synchronises
+    # only its own lane's stream, so the lanes' decode chains overlap on the GPU
+    e0.record(streams[0])
+    for sl in streams[1:]:
+        sl.wait_event(e0)
     for _ in range(args.steps):
         step()
-    e1.record(stream)
+    for ev, sl in zip(ends, streams):
+        ev.record(sl)
+        streams[0].wait_event(ev)
+    e1.record(streams[0])
     m.sync()
     torch.cuda.synchronize(dev)
     dist.barrier()
@@ -334,10 +343,11 @@ def run_ours(args, dist: Dist) -> None:
     hist2 = m.history(n_dec)
     deterministic = bool(np.array_equal(hist, hist2))
 
-    # per-kernel profile at the middle decode position (roofline of the dominant kernel)
+    # per-kernel profile of one lane at the middle decode position (roofline of the dominant kernel)
+    m0 = m.models[0]
     pos_mid = L + n_dec // 2
-    prof = m.profile_decode(pos_mid, iters=20)
-    launches_per_step = m.decode_launches_per_step()
+    prof = m0.profile_decode(pos_mid, iters=20)
+    launches_per_step = m0.decode_launches_per_step()
     step_ms_sum = sum(p["ms"] for p in prof)
     dom = max(prof, key=lambda p: p["ms"])
     peaks = {}
@@ -350,31 +360,46 @@ def run_ours(args, dist: Dist) -> None:
     roof = {"bound": "hbm", "kernel": dom["label"], "achieved": dom_gbs, "peak": hbm, "unit": "GB/s",
             "frac": dom_gbs / hbm, "peak_source": peak_src, "traffic": None,
             "bytes_per_launch": dom["bytes"], "ms_per_launch": dom["ms"], "share_of_step": dom["ms"] / step_ms_sum}
-    step_bytes = sum(p["bytes"] for p in prof)
+    # whole decode launch (all lanes): algorithmic bytes = weights once per lane + KV + acts
+    step_bytes = sum(p["bytes"] for p in prof) * lanes
     step_ms_graph = ms_max / args.steps / n_dec
     whole = {"decode_launch_ms": step_ms_graph, "algorithmic_bytes_per_launch": step_bytes,
              "achieved_gbs": step_bytes / (step_ms_graph / 1e3) / 1e9,
-             "frac_of_hbm": step_bytes / (step_ms_graph / 1e3) / 1e9 / hbm, "kernels_sum_ms": step_ms_sum}
+             "frac_of_hbm": step_bytes / (step_ms_graph / 1e3) / 1e9 / hbm, "lane_kernels_sum_ms": step_ms_sum,
+             "lanes": lanes}
 
-    # e2e: the C-ABI host loop, host token buffers in, host argmax out, per decode launch
-    e2e_steps = max(1, args.e2e_steps)
-    tok = np.ascontiguousarray(first.reshape(B, 1))
-    am = np.zeros(B, np.int32)
-    import ctypes as C
+    # e2e: the C-ABI host loop per lane (one host thread each), host token buffers in, host
+    # argmax out, per decode launch
+    import threading as th
     from llaccel_b200.cuda_backend import _check, _p32
-    lib, sess = m.lib, m._sess
+    e2e_steps = max(1, args.e2e_steps)
+    per = B // lanes
+    outs = [None] * lanes
+
+    def run_lane(li):
+        mm = m.models[li]
+        lib, sess = mm.lib, mm._sess
+        am = np.zeros(per, np.int32)
+        cur = None
+        for _ in range(e2e_steps):
+            cur = np.ascontiguousarray(first[li * per : (li + 1) * per].reshape(per, 1))
+            for i in range(n_dec):
+                _check(lib, lib.llx_run(sess, _p32(cur), 1, L + i, None, 0, None, _p32(am)))
+                cur[:, 0] = am
+        outs[li] = cur[:, 0].copy()
+
     dist.barrier()
     t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        cur = tok.copy()
-        for i in range(n_dec):
-            _check(lib, lib.llx_run(sess, _p32(cur), 1, L + i, None, 0, None, _p32(am)))
-            cur[:, 0] = am
+    threads = [th.Thread(target=run_lane, args=(li,)) for li in range(lanes)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
     e2e_s = dist.max(time.perf_counter() - t0)
-    e2e_ok = bool(np.array_equal(cur[:, 0], hist[n_dec - 1]))
+    e2e_ok = bool(np.array_equal(np.concatenate(outs), hist[n_dec - 1]))
     e2e_value = dist.world * B * n_dec * e2e_steps / e2e_s
-    h2d = n_dec * (B * 4 + 8)
-    d2h = n_dec * (B * 4 + 4)
+    h2d = n_dec * (B * 4 + 8 * lanes)
+    d2h = n_dec * (B * 4 + 8 * lanes)
 
     base = None
     if dist.rank == 0 and not args.no_cpu_baseline:
@@ -387,16 +412,16 @@ def run_ours(args, dist: Dist) -> None:
         "config": {"workload": f"{cfg.name} (Qwen2.5-0.5B arch, QKV bias) decode: {B} seq/GPU, prompt {L}, "
                                f"{n_dec} decode launches/step",
                    "global_batch": B * dist.world, "seq_len": L + n_dec, "prompt": L, "decode_launches": n_dec,
-                   "parallelism": f"dp{dist.world}",
+                   "parallelism": f"dp{dist.world}", "lanes_per_gpu": lanes,
                    "l2": "inputs larger than L2: every decode launch streams ~1 GB of weights + KV",
                    "prefill_s_untimed": prefill_s},
         "roofline": roof, "decode_launch": whole,
         "cpu_baseline": base,
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "steps": e2e_steps, "path": "llx_run per decode launch (C ABI, host buffers)",
+                "steps": e2e_steps, "path": f"llx_run per decode launch (C ABI, host buffers), {lanes} host threads",
                 "tokens_match_device_loop": e2e_ok},
         "clocks": clock,
-        "gpu_launches": launches_per_step * n_dec * args.steps,
+        "gpu_launches": launches_per_step * lanes * n_dec * args.steps,
         "determinism": deterministic,
         "profile_by_kind": _by_kind(prof),
         "profile_top": [{"k": p["label"], "ms": round(p["ms"], 5), "GBs": round(p["bytes"] / max(p["ms"], 1e-9) / 1e6, 1)}

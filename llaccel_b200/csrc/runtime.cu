@@ -826,17 +826,23 @@ static const CUtensorMap& tmap(llx_session* s, const void* base, int64_t rows, i
   return s->tmaps.emplace(key, mp).first->second;
 }
 
-// Tensor-core tiling for R rows x N channels x K.  Enough CTAs to cover the SMs, each
-// with at least two 128-byte K blocks; among those, the widest channel tile (the activation
-// tile is re-read once per channel tile) and the smallest cluster split of K.
+// Tensor-core tiling for R rows x N channels x K: the widest channel tile that alone
+// covers the SMs; else the widest tile that does with K split across a cluster (each CTA
+// keeping at least two 128-byte K blocks); else the narrowest tile, deepest such split.
 static void pick_tc_tiling(int R, int N, int K, int sms, int* nt, int* ksplit) {
   const int row_tiles = (R + 127) / 128;
   const int nkb = (K + 127) / 128;
   const int cands[5] = {256, 128, 64, 32, 16};
   for (int c : cands) {
+    if ((N + c - 1) / c * row_tiles >= sms) {
+      *nt = c;
+      *ksplit = 1;
+      return;
+    }
+  }
+  for (int c : cands) {
     const int tiles = (N + c - 1) / c * row_tiles;
-    for (int ks = 1; ks <= 8; ks *= 2) {
-      if (ks > 1 && nkb / ks < 2) break;
+    for (int ks = 2; ks <= 8 && nkb / ks >= 2; ks *= 2) {
       if (tiles * ks >= sms) {
         *nt = c;
         *ksplit = ks;
@@ -844,7 +850,6 @@ static void pick_tc_tiling(int R, int N, int K, int sms, int* nt, int* ksplit) {
       }
     }
   }
-  // small problem: narrowest tile, deepest split that keeps two K blocks per CTA
   *nt = 16;
   int ks = 1;
   while (ks < 8 && nkb / (ks * 2) >= 2) ks *= 2;

@@ -119,13 +119,21 @@ class CudaModel:
     activation of the last launch readable (needed for `acts=`)."""
 
     def __init__(self, qgraph_dir, *, batch: int = 1, device: int = 0, max_rows: int | None = None,
-                 keep_acts: bool = False, fuse: bool = True, gemm_path: int = 0, pdl: bool = True) -> None:
+                 keep_acts: bool = False, fuse: bool = True, gemm_path: int = 0, pdl: bool = True,
+                 share: "CudaModel | None" = None) -> None:
+        """`share`: reuse the weights already loaded by another CudaModel (same device); this
+        instance then owns only its session (KV cache, activations, stream)."""
         self.lib = load_library()
         self.dir = Path(qgraph_dir)
         self.batch = int(batch)
-        opts = LlxOpts(int(device), 1 if fuse else 0, int(gemm_path), 1 if pdl else 0)
-        self._model = C.c_void_p()
-        _check(self.lib, self.lib.llx_model_load(str(self.dir).encode(), C.byref(opts), C.byref(self._model)))
+        self._owns_model = share is None
+        if share is not None:
+            self._model = share._model
+            self._shared_from = share  # keeps the owner alive
+        else:
+            opts = LlxOpts(int(device), 1 if fuse else 0, int(gemm_path), 1 if pdl else 0)
+            self._model = C.c_void_p()
+            _check(self.lib, self.lib.llx_model_load(str(self.dir).encode(), C.byref(opts), C.byref(self._model)))
         info = LlxModelInfo()
         _check(self.lib, self.lib.llx_model_get_info(self._model, C.byref(info)))
         self.info = info
@@ -147,7 +155,8 @@ class CudaModel:
             self.lib.llx_session_destroy(self._sess)
             self._sess = None
         if getattr(self, "_model", None):
-            self.lib.llx_model_destroy(self._model)
+            if getattr(self, "_owns_model", True):
+                self.lib.llx_model_destroy(self._model)
             self._model = None
 
     def __del__(self):  # pragma: no cover
@@ -387,3 +396,48 @@ class CudaModel:
         if n < 0:
             raise LlxError(LLX_ERR_CUDA, self.lib.llx_last_error().decode())
         return n
+
+
+class CudaLanes:
+    """`lanes` sessions over one loaded model, each holding batch/lanes of the sequences on
+    its own CUDA stream.  Decode steps of different lanes are independent, so their kernel
+    chains run concurrently and fill the GPU where one chain alone is latency-bound.
+    Results are those of one session holding every sequence (sequences never interact)."""
+
+    def __init__(self, qgraph_dir, *, batch: int, lanes: int, device: int = 0, max_rows: int | None = None,
+                 **kw) -> None:
+        if lanes < 1 or batch % lanes:
+            raise ValueError("batch must be a multiple of lanes")
+        self.batch, self.lanes, self.per = batch, lanes, batch // lanes
+        first = CudaModel(qgraph_dir, batch=self.per, device=device, max_rows=max_rows, **kw)
+        self.models = [first] + [CudaModel(qgraph_dir, batch=self.per, device=device, max_rows=max_rows, share=first)
+                                 for _ in range(lanes - 1)]
+
+    def generate_batch(self, prompts, n_tokens: int, **kw) -> list[dict]:
+        out = []
+        for i, m in enumerate(self.models):
+            out.extend(m.generate_batch(prompts[i * self.per : (i + 1) * self.per], n_tokens, **kw))
+        return out
+
+    def set_tokens(self, tokens) -> None:
+        t = np.asarray(tokens, dtype=np.int32).reshape(self.lanes, self.per)
+        for m, tl in zip(self.models, t):
+            m.set_tokens(tl)
+
+    def decode_async(self, pos: int, n_steps: int) -> None:
+        for m in self.models:
+            m.decode_async(pos, n_steps)
+
+    def sync(self) -> None:
+        for m in self.models:
+            m.sync()
+
+    def history(self, n_steps: int) -> np.ndarray:
+        return np.concatenate([m.history(n_steps) for m in self.models], axis=1)
+
+    def streams(self) -> list[int]:
+        return [m.stream_handle() for m in self.models]
+
+    def close(self) -> None:
+        for m in reversed(self.models):
+            m.close()

@@ -181,3 +181,26 @@ def test_invalid_qgraphs_are_rejected(tmp_path):
         (d / "qgraph.json").write_text(json.dumps(g))
         with pytest.raises(ValueError, match=match):
             CudaModel(d)
+
+
+def test_lanes_equal_one_session():
+    """Lanes (sessions sharing one loaded model, one stream each) decode exactly like one
+    session holding every sequence."""
+    from llaccel_b200.cuda_backend import CudaLanes
+    d = GOLDEN / "c1_v2"
+    B, L, n = 8, 20, 12
+    prompts = np.random.default_rng(11).integers(0, 512, (B, L)).tolist()
+    with CudaModel(d, batch=B) as one:
+        want = one.generate_batch(prompts, n)
+    lanes = CudaLanes(d, batch=B, lanes=4)
+    try:
+        got = lanes.generate_batch(prompts, n)
+        assert got == want
+        lanes.set_tokens([r["generated"][0] for r in want])
+        lanes.decode_async(L, n - 1)
+        lanes.sync()
+        h = lanes.history(n - 1)
+        for b in range(B):
+            assert h[:, b].tolist() == want[b]["argmax_per_step"][2 : 2 + n - 1]
+    finally:
+        lanes.close()
