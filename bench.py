@@ -55,7 +55,7 @@ def parse_args():
     ap.add_argument("--cpu-decode", type=int, default=8, help="decode launches in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gemm-path", type=int, default=0)
-    ap.add_argument("--lanes", type=int, default=4, help="concurrent decode lanes (sub-batches on own streams)")
+    ap.add_argument("--lanes", type=int, default=1, help="concurrent decode lanes (sub-batches on own streams)")
     return ap.parse_args()
 
 
@@ -343,6 +343,48 @@ def run_ours(args, dist: Dist) -> None:
     hist2 = m.history(n_dec)
     deterministic = bool(np.array_equal(hist, hist2))
 
+    # e2e: the C-ABI host loop per lane (one host thread each), host token buffers in, host
+    # argmax out, per decode launch
+    import threading as th
+    from llaccel_b200.cuda_backend import _check, _p32
+    e2e_steps = max(1, args.e2e_steps)
+    per = B // lanes
+    outs = [None] * lanes
+
+    trace = [None] * lanes
+
+    def run_lane(li):
+        mm = m.models[li]
+        lib, sess = mm.lib, mm._sess
+        am = np.zeros(per, np.int32)
+        cur = None
+        tr = np.zeros((n_dec, per), np.int32)
+        for _ in range(e2e_steps):
+            cur = np.ascontiguousarray(first[li * per : (li + 1) * per].reshape(per, 1))
+            for i in range(n_dec):
+                _check(lib, lib.llx_run(sess, _p32(cur), 1, L + i, None, 0, None, _p32(am)))
+                cur[:, 0] = am
+                tr[i] = am
+        outs[li] = cur[:, 0].copy()
+        trace[li] = tr
+
+    dist.barrier()
+    t0 = time.perf_counter()
+    threads = [th.Thread(target=run_lane, args=(li,)) for li in range(lanes)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    e2e_s = dist.max(time.perf_counter() - t0)
+    e2e_trace = np.concatenate(trace, axis=1)
+    e2e_ok = bool(np.array_equal(e2e_trace, hist))
+    bad_steps = np.nonzero((e2e_trace != hist).any(axis=1))[0]
+    e2e_diag = {"mismatch_steps": int(len(bad_steps)), "first_bad_step": int(bad_steps[0]) if len(bad_steps) else None,
+                "mismatch_tokens": int((e2e_trace != hist).sum())}
+    e2e_value = dist.world * B * n_dec * e2e_steps / e2e_s
+    h2d = n_dec * (B * 4 + 8 * lanes)
+    d2h = n_dec * (B * 4 + 8 * lanes)
+
     # per-kernel profile of one lane at the middle decode position (roofline of the dominant kernel)
     m0 = m.models[0]
     pos_mid = L + n_dec // 2
@@ -368,39 +410,6 @@ def run_ours(args, dist: Dist) -> None:
              "frac_of_hbm": step_bytes / (step_ms_graph / 1e3) / 1e9 / hbm, "lane_kernels_sum_ms": step_ms_sum,
              "lanes": lanes}
 
-    # e2e: the C-ABI host loop per lane (one host thread each), host token buffers in, host
-    # argmax out, per decode launch
-    import threading as th
-    from llaccel_b200.cuda_backend import _check, _p32
-    e2e_steps = max(1, args.e2e_steps)
-    per = B // lanes
-    outs = [None] * lanes
-
-    def run_lane(li):
-        mm = m.models[li]
-        lib, sess = mm.lib, mm._sess
-        am = np.zeros(per, np.int32)
-        cur = None
-        for _ in range(e2e_steps):
-            cur = np.ascontiguousarray(first[li * per : (li + 1) * per].reshape(per, 1))
-            for i in range(n_dec):
-                _check(lib, lib.llx_run(sess, _p32(cur), 1, L + i, None, 0, None, _p32(am)))
-                cur[:, 0] = am
-        outs[li] = cur[:, 0].copy()
-
-    dist.barrier()
-    t0 = time.perf_counter()
-    threads = [th.Thread(target=run_lane, args=(li,)) for li in range(lanes)]
-    for t in threads:
-        t.start()
-    for t in threads:
-        t.join()
-    e2e_s = dist.max(time.perf_counter() - t0)
-    e2e_ok = bool(np.array_equal(np.concatenate(outs), hist[n_dec - 1]))
-    e2e_value = dist.world * B * n_dec * e2e_steps / e2e_s
-    h2d = n_dec * (B * 4 + 8 * lanes)
-    d2h = n_dec * (B * 4 + 8 * lanes)
-
     base = None
     if dist.rank == 0 and not args.no_cpu_baseline:
         base = cpu_baseline(qdir, prompts[0], min(args.cpu_decode, n_dec), hist[:, 0])
@@ -419,7 +428,7 @@ def run_ours(args, dist: Dist) -> None:
         "cpu_baseline": base,
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "steps": e2e_steps, "path": f"llx_run per decode launch (C ABI, host buffers), {lanes} host threads",
-                "tokens_match_device_loop": e2e_ok},
+                "tokens_match_device_loop": e2e_ok, **e2e_diag},
         "clocks": clock,
         "gpu_launches": launches_per_step * lanes * n_dec * args.steps,
         "determinism": deterministic,

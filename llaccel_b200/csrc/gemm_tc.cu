@@ -436,6 +436,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (a.q_out) store16_i8(a.q_out + off, fq, cnt);
       }
     } else {
+      unsigned long long best = 0ull;  // fused argmax key of this thread's row
 #pragma unroll 1
       for (int ci = 0; ci < NT / 16; ++ci) {
         if (ci % ksplit != (int)crank || (ci / ksplit) % 2 != half) continue;
@@ -482,7 +483,19 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int j = 0; j < 16; ++j) o[j] = silu_fast(o[j], Mi, a.silu_Si, a.silu_sh, s_sig);
         }
         store16_i16(reinterpret_cast<int16_t*>(dst) + (int64_t)r * ld + col, o, cnt);
+        if (a.amax_key) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int n = nb + j;
+            if (j < cnt && n < a.amax_vocab) {
+              const unsigned long long key =
+                  ((unsigned long long)(uint32_t)(o[j] + 32768) << 32) | (0xFFFFFFFFu - (uint32_t)n);
+              best = key > best ? key : best;
+            }
+          }
+        }
       }
+      if (a.amax_key && best && r < a.R) atomicMax(a.amax_key + r, best);
     }
   }
   if (ksplit > 1) cluster_sync();  // peers keep their shared memory until rank 0 has read it

@@ -12,8 +12,11 @@ namespace llx {
 
 // ---- vector engine ----------------------------------------------------------------------
 // tokens [R] (< 0 = zero pad row) -> out [R][dim] i16 rows of `embed`
+// also zeroes amax_key[0..R) when non-null (the fused argmax of the output linear)
 cudaError_t launch_embed(const int32_t* tokens, const int16_t* embed, int16_t* out, int R, int dim, int vocab_rows,
-                         int32_t* err, cudaStream_t st);
+                         int32_t* err, unsigned long long* amax_key, cudaStream_t st);
+// argmax tokens from the fused argmax keys: out[r] = 0xFFFFFFFF - low32(key[r])
+cudaError_t launch_amax_finish(const unsigned long long* keys, int32_t* out, int R, cudaStream_t st);
 
 // rows x [nrows][K] -> y [nrows][K]; optional fused quant to y8 (M_q, S_q)
 cudaError_t launch_rmsnorm(const int16_t* x, const int16_t* gamma, int16_t* y, int8_t* y8, int nrows, int K,
@@ -95,6 +98,11 @@ struct LinearArgs {
   int8_t* q_out;
   int64_t q_M;
   int q_S;
+  // Fused argmax (model output linear): per row, the max over channels n < amax_vocab of
+  // key = (logit + 32768) << 32 | (0xFFFFFFFF - n) is folded into amax_key[r] with a 64-bit
+  // atomicMax (largest logit, lowest index on ties).  amax_key must be zero beforehand.
+  unsigned long long* amax_key;
+  int amax_vocab;
 };
 
 // CUDA-core paths: 0 = auto, 1 = GEMV (small R), 2 = tiled dp4a

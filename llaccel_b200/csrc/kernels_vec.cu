@@ -20,10 +20,12 @@ static inline unsigned grid1d(int64_t n, int per_block) { return (unsigned)((n +
 
 // ---- embedding gather (golden.py:369-373; host.cpp:108-113) ------------------------------
 __global__ void k_embed(const int32_t* __restrict__ tokens, const int16_t* __restrict__ embed,
-                        int16_t* __restrict__ out, int R, int dim, int vocab_rows, int32_t* err) {
+                        int16_t* __restrict__ out, int R, int dim, int vocab_rows, int32_t* err,
+                        unsigned long long* __restrict__ amax_key) {
   pdl_trigger();
   pdl_wait();
   const int r = blockIdx.x;
+  if (amax_key && threadIdx.x == 0) amax_key[r] = 0ull;
   const int tok = tokens[r];
   const int chunks = dim / 8;
   uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)r * dim);
@@ -37,9 +39,24 @@ __global__ void k_embed(const int32_t* __restrict__ tokens, const int16_t* __res
 }
 
 cudaError_t launch_embed(const int32_t* tokens, const int16_t* embed, int16_t* out, int R, int dim, int vocab_rows,
-                         int32_t* err, cudaStream_t st) {
+                         int32_t* err, unsigned long long* amax_key, cudaStream_t st) {
   if (R <= 0) return cudaSuccess;
-  { const cudaError_t e_ = launch_k(k_embed, dim3(R), dim3(64), 0, st, tokens, embed, out, R, dim, vocab_rows, err); if (e_ != cudaSuccess) return e_; }
+  { const cudaError_t e_ = launch_k(k_embed, dim3(R), dim3(64), 0, st, tokens, embed, out, R, dim, vocab_rows, err,
+                                    amax_key); if (e_ != cudaSuccess) return e_; }
+  return cudaGetLastError();
+}
+
+__global__ void k_amax_finish(const unsigned long long* __restrict__ keys, int32_t* __restrict__ out, int R) {
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < R) out[r] = (int32_t)(0xFFFFFFFFu - (uint32_t)(keys[r] & 0xFFFFFFFFull));
+}
+
+cudaError_t launch_amax_finish(const unsigned long long* keys, int32_t* out, int R, cudaStream_t st) {
+  if (R <= 0) return cudaSuccess;
+  { const cudaError_t e_ = launch_k(k_amax_finish, dim3((R + 255) / 256), dim3(256), 0, st, keys, out, R);
+    if (e_ != cudaSuccess) return e_; }
   return cudaGetLastError();
 }
 

@@ -789,6 +789,7 @@ struct llx_session {
   size_t tail_rows_alloc = 0;
   std::map<std::tuple<const void*, int64_t, int64_t, int>, CUtensorMap> tmaps;
   int32_t* d_fault = nullptr;  // nonzero: a tensor-core pipeline wait timed out
+  unsigned long long* d_amax_key = nullptr;  // [B*max_rows] fused argmax keys of the output linear
   cudaGraphExec_t decode_exec = nullptr;
   int decode_launches = 0;
   int last_R = 0, last_Rtail = 0;
@@ -871,6 +872,20 @@ static int gemm_path_for(const llx_model* m, int R) {
   return path;
 }
 
+// The model output is a plain linear on the tensor-core path: its epilogue produced the
+// argmax keys, which only need decoding; otherwise a full argmax pass over the logits runs.
+static bool output_argmax_fused(const llx_model* m, int R) {
+  for (const Step& x : m->steps)
+    if (x.kind == SK::Linear && x.out == m->output_act) return gemm_path_for(m, R) == 3;
+  return false;
+}
+
+static cudaError_t launch_output_argmax(llx_session* s, const void* logits, int R) {
+  const llx_model* m = s->m;
+  if (output_argmax_fused(m, R)) return launch_amax_finish(s->d_amax_key, s->d_argmax, R, s->st);
+  return launch_argmax((const int16_t*)logits, R, m->vocab_padded, m->vocab, s->d_argmax, s->st);
+}
+
 static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, int M) {
   llx_model* m = s->m;
   cudaStream_t st = s->st;
@@ -880,7 +895,7 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
     switch (x.kind) {
       case SK::Embed:
         e = launch_embed(s->d_tokens, (const int16_t*)dptr(m, m->embed_off), (int16_t*)P(x.out), R, m->dim,
-                         m->vocab, s->d_err, st);
+                         m->vocab, s->d_err, s->d_amax_key, st);
         break;
       case SK::RmsNorm:
         e = launch_rmsnorm((const int16_t*)P(x.in), (const int16_t*)dptr(m, x.gamma_off), (int16_t*)P(x.out),
@@ -909,6 +924,10 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
         a.luts = m->d_luts;
         a.narrow = x.narrow;
         const int path = gemm_path_for(m, R);
+        if (path == 3 && x.out == m->output_act) {
+          a.amax_key = s->d_amax_key;
+          a.amax_vocab = m->vocab;
+        }
         if (path == 3) {
           int nt = 16, ks = 1;
           pick_tc_tiling(R, x.N, x.K, m->sms, &nt, &ks);
@@ -1218,8 +1237,7 @@ static void run_launch(llx_session* s, int M, int pos, bool with_embed, const in
     }
     enqueue_steps(s, bt, m->tail_start, m->steps.size(), Rtail, n_rec);
   }
-  const cudaError_t e = launch_argmax((const int16_t*)bd.p[m->output_act], Rtail, m->vocab_padded, m->vocab,
-                                      s->d_argmax, s->st);
+  const cudaError_t e = launch_output_argmax(s, bd.p[m->output_act], Rtail);
   if (e != cudaSuccess) throw Error(LLX_ERR_CUDA, cudaGetErrorString(e));
   s->last_R = R;
   s->last_Rtail = Rtail;
@@ -1259,8 +1277,7 @@ static void build_decode_graph(llx_session* s) {
   int n = 0;
   try {
     n = enqueue_steps(s, bd, 0, m->steps.size(), s->B, 1);
-    cudaError_t e = launch_argmax((const int16_t*)bd.p[m->output_act], s->B, m->vocab_padded, m->vocab, s->d_argmax,
-                                  s->st);
+    cudaError_t e = launch_output_argmax(s, bd.p[m->output_act], s->B);
     if (e != cudaSuccess) throw Error(LLX_ERR_CUDA, cudaGetErrorString(e));
     LLX_CUDA(launch_k(k_decode_finalize, dim3(1), dim3(256), 0, s->st, (const int32_t*)s->d_argmax, s->d_tokens,
                       s->d_hist, s->d_pos, s->d_step, s->B, s->hist_cap));
@@ -1306,6 +1323,8 @@ static void session_create(llx_model* m, int batch, int max_rows, int keep, llx_
   LLX_CUDA(cudaMalloc(&s->d_tokens, sizeof(int32_t) * rows));
   LLX_CUDA(cudaMalloc(&s->d_rec, sizeof(int32_t) * rows));
   LLX_CUDA(cudaMalloc(&s->d_argmax, sizeof(int32_t) * rows));
+  LLX_CUDA(cudaMalloc(&s->d_amax_key, sizeof(unsigned long long) * rows));
+  LLX_CUDA(cudaMemset(s->d_amax_key, 0, sizeof(unsigned long long) * rows));
   LLX_CUDA(cudaMalloc(&s->d_hist, sizeof(int32_t) * (size_t)s->hist_cap * batch));
   LLX_CUDA(cudaMalloc(&s->d_pos, sizeof(int32_t) * 4));
   s->d_step = s->d_pos + 1;
@@ -1325,7 +1344,7 @@ static void session_free(llx_session* s) {
   if (s->st) cudaStreamSynchronize(s->st);
   if (s->decode_exec) cudaGraphExecDestroy(s->decode_exec);
   for (void* p : {(void*)s->arena, (void*)s->kv, (void*)s->d_tokens, (void*)s->d_rec, (void*)s->d_argmax,
-                  (void*)s->d_hist, (void*)s->d_pos})
+                  (void*)s->d_hist, (void*)s->d_pos, (void*)s->d_amax_key})
     if (p) cudaFree(p);
   for (void* p : {(void*)s->h_tok, (void*)s->h_rec, (void*)s->h_am, (void*)s->h_pos, (void*)s->h_i16})
     if (p) cudaFreeHost(p);
@@ -1493,6 +1512,7 @@ llx_status llx_run_rows(llx_session* s, const int16_t* rows, int M, int pos, int
     std::memcpy(s->h_i16, rows, n * sizeof(int16_t));
     const Binding bd = bind(s, false);
     LLX_CUDA(cudaMemcpyAsync(bd.p[s->m->input_act], s->h_i16, n * sizeof(int16_t), cudaMemcpyHostToDevice, s->st));
+    LLX_CUDA(cudaMemsetAsync(s->d_amax_key, 0, sizeof(unsigned long long) * s->B * M, s->st));
     run_launch(s, M, pos, false, nullptr, M);
     copy_outputs(s, s->B * M, logits, argmax);
   });
@@ -1714,7 +1734,7 @@ llx_status llx_profile_decode(llx_session* s, int pos, int iters, float* ms, dou
             break;
         }
       } else {
-        b = 2.0 * R * m->vocab_padded + 4.0 * R;
+        b = output_argmax_fused(m, R) ? 12.0 * R : 2.0 * R * m->vocab_padded + 4.0 * R;
       }
       // one untimed launch, then `iters` timed launches
       for (int it = 0; it <= iters; ++it) {
@@ -1722,8 +1742,7 @@ llx_status llx_profile_decode(llx_session* s, int pos, int iters, float* ms, dou
         if (i < (int)m->steps.size()) {
           enqueue_steps(s, bd, i, i + 1, R, 1);
         } else {
-          const cudaError_t e = launch_argmax((const int16_t*)bd.p[m->output_act], R, m->vocab_padded, m->vocab,
-                                              s->d_argmax, s->st);
+          const cudaError_t e = launch_output_argmax(s, bd.p[m->output_act], R);
           if (e != cudaSuccess) throw Error(LLX_ERR_CUDA, cudaGetErrorString(e));
         }
       }
