@@ -381,6 +381,9 @@ def run_ours(args, dist: Dist) -> None:
     bad_steps = np.nonzero((e2e_trace != hist).any(axis=1))[0]
     e2e_diag = {"mismatch_steps": int(len(bad_steps)), "first_bad_step": int(bad_steps[0]) if len(bad_steps) else None,
                 "mismatch_tokens": int((e2e_trace != hist).sum())}
+    if len(bad_steps):
+        e2e_diag["step0_e2e"] = e2e_trace[0, :8].tolist()
+        e2e_diag["step0_dev"] = hist[0, :8].tolist()
     e2e_value = dist.world * B * n_dec * e2e_steps / e2e_s
     h2d = n_dec * (B * 4 + 8 * lanes)
     d2h = n_dec * (B * 4 + 8 * lanes)

@@ -204,3 +204,25 @@ def test_lanes_equal_one_session():
             assert h[:, b].tolist() == want[b]["argmax_per_step"][2 : 2 + n - 1]
     finally:
         lanes.close()
+
+
+@pytest.mark.parametrize("name,B", [("c1_v2", 4), ("c1_v2", 20), ("qwen2_tiny", 16)])
+def test_host_driven_batch_decode_matches_device_loop(name, B):
+    """llx_run with batch > 1 and M = 1 (the C-ABI host loop) == the device-resident loop."""
+    import ctypes as C
+    from llaccel_b200.cuda_backend import _check, _p32
+    o = O.OracleModel(GOLDEN / name)
+    L, n = 20, 10
+    prompts = np.random.default_rng(B).integers(0, o.vocab, (B, L)).tolist()
+    with CudaModel(GOLDEN / name, batch=B) as m:
+        recs = m.generate_batch(prompts, n)
+        first = np.array([r["generated"][0] for r in recs], np.int32)
+        cur = first.reshape(B, 1).copy()
+        am = np.zeros(B, np.int32)
+        host = []
+        for i in range(n - 1):
+            _check(m.lib, m.lib.llx_run(m._sess, _p32(cur), 1, L + i, None, 0, None, _p32(am)))
+            host.append(am.copy())
+            cur[:, 0] = am
+        for b in range(B):
+            assert [h[b] for h in host] == recs[b]["argmax_per_step"][2 : 2 + n - 1], b
