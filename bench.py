@@ -360,7 +360,7 @@ def run_ours(args, dist: Dist) -> None:
         cur = None
         tr = np.zeros((n_dec, per), np.int32)
         for _ in range(e2e_steps):
-            cur = np.ascontiguousarray(first[li * per : (li + 1) * per].reshape(per, 1))
+            cur = first[li * per : (li + 1) * per].reshape(per, 1).copy()  # never a view of `first`
             for i in range(n_dec):
                 _check(lib, lib.llx_run(sess, _p32(cur), 1, L + i, None, 0, None, _p32(am)))
                 cur[:, 0] = am
