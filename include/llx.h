@@ -129,6 +129,22 @@ llx_status llx_read_activation(llx_session* s, const char* name, void* dst, size
 const char* llx_last_error(void);
 const char* llx_version(void);
 
+/* Output projection with fused argmax that allocates no device memory.
+ * No counterpart in the reference: it exists for callers that cannot call cudaMalloc --
+ * code running inside another framework's memory pool, plugin hosts that only hand out
+ * pre-sized buffers, processes that must not grow their device footprint after start-up.
+ * The caller passes device buffers for everything: A [R][K] i8, W [N][K] i8, bias [N] i32
+ * (may be NULL), rq [N][2] i32, logits [R][N] i16 (out), argmax [R] i32 (out, over the first
+ * `vocab` channels, lowest index on ties).  Semantics are those of a qgraph linear with
+ * epilogue none followed by the argmax of golden.py:376.  The per-row argmax keys use a
+ * fixed file-scope device array of 4096 rows held by every GPU that loads the library until
+ * exit: R > 4096 is rejected with LLX_ERR_RANGE.  The call is synchronous on `stream`
+ * (a cudaStream_t, NULL = default stream).  Its first call on a device looks up that
+ * array's device address and sets kernel attributes, so make it before any stream capture.
+ * All calls share the array: calls that overlap on the GPU race. */
+llx_status llx_linear_argmax_noalloc(const int8_t* A, const int8_t* W, const int32_t* bias, const int32_t* rq, int R,
+                                     int N, int K, int vocab, int16_t* logits, int32_t* argmax, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

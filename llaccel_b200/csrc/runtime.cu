@@ -38,6 +38,9 @@ namespace llx {
 
 static thread_local std::string g_err;
 
+// error text of llx_linear_argmax_noalloc (noalloc.cu), read back by llx_last_error
+void noalloc_set_error(const std::string& msg) { g_err = msg; }
+
 struct Error : std::runtime_error {
   llx_status code;
   Error(llx_status c, const std::string& m) : std::runtime_error(m), code(c) {}

@@ -54,6 +54,8 @@ SIGNATURES = {
     "llx_activation_name": (C.c_char_p, [C.c_void_p, C.c_int]),
     "llx_activation_shape": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "llx_read_activation": (C.c_int, [C.c_void_p, C.c_char_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_int)]),
+    "llx_linear_argmax_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                            C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
     "llx_last_error": (C.c_char_p, []),
     "llx_version": (C.c_char_p, []),
 }
