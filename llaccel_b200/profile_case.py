@@ -1,0 +1,43 @@
+"""A small decode case for profilers: one of the bench configs with a short prompt, so a
+capture holds a few GB on the device at most and ends by itself.
+
+    python -m llaccel_b200.profile_case --config c3 --batch 128 --prompt 32 --decode 3
+
+Generates (or reuses) the config's artefact under --artefacts, prefills `batch` random
+prompts of `prompt` tokens, then runs `decode` device-resident decode launches and prints
+the first sequence's tokens.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import tempfile
+from pathlib import Path
+
+import numpy as np
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--config", default="c3")
+    ap.add_argument("--batch", type=int, default=128)
+    ap.add_argument("--prompt", type=int, default=32)
+    ap.add_argument("--decode", type=int, default=3)
+    ap.add_argument("--artefacts", default=os.environ.get("LLX_ARTEFACTS", str(Path(tempfile.gettempdir()) / "llx_artefacts")))
+    a = ap.parse_args(argv)
+    from llaccel_b200 import artefacts as A, build
+    build.build()
+    from llaccel_b200.cuda_backend import CudaModel
+    d = A.ensure_artefact(a.config, a.artefacts, seed=0, fusion=True, device="cuda")
+    m = CudaModel(d, batch=a.batch, max_rows=a.prompt)
+    prompts = np.random.default_rng(0).integers(0, A.CONFIGS[a.config].vocab, (a.batch, a.prompt)).tolist()
+    recs = m.generate_batch(prompts, 0, with_logits=False)
+    m.set_tokens([r["argmax_per_step"][-1] for r in recs])
+    m.decode_async(a.prompt, a.decode)
+    m.sync()
+    print("ok", m.history(a.decode)[:, 0].tolist())
+    m.close()
+
+
+if __name__ == "__main__":
+    main()
