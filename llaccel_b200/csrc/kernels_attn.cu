@@ -133,7 +133,10 @@ constexpr int kDecThreads = 256, kDecWarps = kDecThreads / 32;
 
 size_t attention_decode_smem_bytes(int H, int Hkv, int D, int max_seq) {
   const int rep = H / Hkv;
-  return (size_t)rep * max_seq * 4 + (size_t)kDecWarps * rep * D * 4 + (size_t)rep * D + 64;
+  // scores / probabilities (i32), normalised probabilities (i16), per-warp partial sums of
+  // the value pass, q rows, per-warp head maxima and sums
+  return (size_t)rep * D + (size_t)rep * max_seq * 4 + (size_t)rep * (size_t)((max_seq + 3) & ~1) * 2 +
+         (size_t)kDecWarps * rep * D * 4 + (size_t)kDecWarps * rep * 8 + 64;
 }
 
 __device__ __forceinline__ int dot16_i8(const uint4& a, const uint4& b, int acc) {
@@ -150,13 +153,17 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
     int H, int Hkv, int max_seq, const int* __restrict__ d_pos, int64_t Ms, int Ss, int64_t Mo, int So, int prob_bits,
     const uint16_t* __restrict__ luts) {
   constexpr int D = LPK * 16;
-  constexpr int KPW = 32 / LPK;  // keys per warp per iteration
+  constexpr int KPW = 32 / LPK;  // key rows per warp per step
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ uint16_t s_expi[16], s_expf[256];
   const int rep = H / Hkv;
-  int32_t* sc = reinterpret_cast<int32_t*>(smem);                       // [rep][max_seq]
-  int32_t* red = sc + (size_t)rep * max_seq;                             // [warps][rep][D]
-  int8_t* q_s = reinterpret_cast<int8_t*>(red + (size_t)kDecWarps * rep * D);  // [rep][D]
+  const int pstride = (max_seq + 3) & ~1;                                // i16 row stride (even, > max_seq)
+  int8_t* q_s = reinterpret_cast<int8_t*>(smem);                         // [rep][D] (16-byte rows)
+  int32_t* sc = reinterpret_cast<int32_t*>(q_s + rep * D);               // [rep][max_seq] scores, then p
+  int16_t* pn16 = reinterpret_cast<int16_t*>(sc + (size_t)rep * max_seq);  // [rep][pstride] normalised p
+  int32_t* red = reinterpret_cast<int32_t*>(pn16 + (size_t)rep * pstride);  // [warps][rep][D]
+  int32_t* wmax = red + (size_t)kDecWarps * rep * D;                     // [warps][rep]
+  uint32_t* wsum = reinterpret_cast<uint32_t*>(wmax + kDecWarps * rep);  // [warps][rep]
   const int b = blockIdx.x, kvh = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane % LPK, kg = lane / LPK;
@@ -178,13 +185,18 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   const int8_t* vbase = vc + ((int64_t)b * Hkv + kvh) * max_seq * D;
   const int stride = kDecWarps * KPW;
 
-  // ---- scores ----
+  // ---- scores, with each head's running maximum ----
+  int32_t mxl[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) mxl[j] = INT_MIN;
   for (int t0 = warp * KPW; t0 < T; t0 += 2 * stride) {
     const int ta = t0 + kg, tb = t0 + stride + kg;
     uint4 ka = make_uint4(0, 0, 0, 0), kb = make_uint4(0, 0, 0, 0);
     if (ta < T) ka = __ldg(reinterpret_cast<const uint4*>(kbase + (int64_t)ta * D) + sub);
     if (tb < T) kb = __ldg(reinterpret_cast<const uint4*>(kbase + (int64_t)tb * D) + sub);
-    for (int j = 0; j < rep; ++j) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (j >= rep) break;
       const uint4 qv = reinterpret_cast<const uint4*>(q_s + j * D)[sub];
       int sa = dot16_i8(ka, qv, 0), sb = dot16_i8(kb, qv, 0);
 #pragma unroll
@@ -192,55 +204,93 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
         sa += __shfl_xor_sync(0xffffffffu, sa, o);
         sb += __shfl_xor_sync(0xffffffffu, sb, o);
       }
-      if (sub == 0) {
-        if (ta < T) sc[j * max_seq + ta] = sa;
-        if (tb < T) sc[j * max_seq + tb] = sb;
+      if (ta < T) {
+        mxl[j] = max(mxl[j], sa);
+        if (sub == 0) sc[j * max_seq + ta] = sa;
+      }
+      if (tb < T) {
+        mxl[j] = max(mxl[j], sb);
+        if (sub == 0) sc[j * max_seq + tb] = sb;
       }
     }
   }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if (j >= rep) break;
+    int32_t v = mxl[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) wmax[warp * rep + j] = v;
+  }
   __syncthreads();
 
-  // ---- max, exp-sum, normalised probabilities: one warp per head ----
+  // ---- exp LUT probabilities and their sums (all threads, heads outer) ----
   const int pmax = (1 << prob_bits) - 1, pshift = 31 - prob_bits;
-  for (int j = warp; j < rep; j += kDecWarps) {
+  for (int j = 0; j < rep; ++j) {
+    int32_t mx = wmax[j];
+    for (int w = 1; w < kDecWarps; ++w) mx = max(mx, wmax[w * rep + j]);
     int32_t* s = sc + j * max_seq;
-    int32_t mx = INT_MIN;
-    for (int t = lane; t < T; t += 32) mx = max(mx, s[t]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     uint32_t sum = 0;
-    for (int t = lane; t < T; t += 32) {
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
       const uint32_t p = exp_prob(mulshift((int64_t)mx - s[t], Ms, Ss), s_expi, s_expf);
       s[t] = (int32_t)p;
       sum += p;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) wsum[warp * rep + j] = sum;
+  }
+  __syncthreads();
+  // ---- normalised probabilities (Q0.15 or Q0.8) as i16, zero past the last key ----
+  for (int j = 0; j < rep; ++j) {
+    uint32_t sum = 0;
+    for (int w = 0; w < kDecWarps; ++w) sum += wsum[w * rep + j];
     const int64_t inv = udiv((uint64_t)1 << 31, sum);
-    for (int t = lane; t < T; t += 32) {
-      const int64_t pn = rshr((int64_t)s[t] * inv, pshift);
-      s[t] = (int32_t)(pn < pmax ? pn : pmax);
+    const int32_t* s = sc + j * max_seq;
+    int16_t* pj = pn16 + (size_t)j * pstride;
+    for (int t = threadIdx.x; t < T + 2; t += blockDim.x) {
+      int32_t v = 0;
+      if (t < T) {
+        const int64_t pn = rshr((int64_t)s[t] * inv, pshift);
+        v = (int32_t)(pn < pmax ? pn : pmax);
+      }
+      if (t < pstride) pj[t] = (int16_t)v;
     }
   }
   __syncthreads();
 
-  // ---- o[j][d] = sum_t pn[j][t] * v[t][d], RB heads per pass ----
+  // ---- o[j][d] = sum_t pn[j][t] * v[t][d]: key pairs through dp2a, RB heads per pass ----
   int8_t* orow = out + ((int64_t)b * H + (int64_t)kvh * rep) * D;
+  const int pair_stride = kDecWarps * KPW * 2;
   for (int j0 = 0; j0 < rep; j0 += RB) {
     int32_t acc[RB][16];
 #pragma unroll
     for (int r = 0; r < RB; ++r)
 #pragma unroll
       for (int i = 0; i < 16; ++i) acc[r][i] = 0;
-    for (int t = warp * KPW + kg; t < T; t += stride) {
-      const uint4 vv = __ldg(reinterpret_cast<const uint4*>(vbase + (int64_t)t * D) + sub);
-      const uint32_t w[4] = {vv.x, vv.y, vv.z, vv.w};
+    for (int t = (warp * KPW + kg) * 2; t < T; t += pair_stride) {
+      const uint4 va = __ldg(reinterpret_cast<const uint4*>(vbase + (int64_t)t * D) + sub);
+      uint4 vb = make_uint4(0, 0, 0, 0);
+      if (t + 1 < T) vb = __ldg(reinterpret_cast<const uint4*>(vbase + (int64_t)(t + 1) * D) + sub);
+      // (v_t[d], v_t+1[d]) byte pairs: x[2k] holds d = 4k, 4k+1; x[2k+1] holds d = 4k+2, 4k+3
+      const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
+      uint32_t x[8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        x[2 * k] = __byte_perm(wa[k], wb[k], 0x5140);
+        x[2 * k + 1] = __byte_perm(wa[k], wb[k], 0x7362);
+      }
 #pragma unroll
       for (int r = 0; r < RB; ++r) {
         const int j = j0 + r;
-        const int32_t pn = j < rep ? sc[j * max_seq + t] : 0;
+        if (j >= rep) break;
+        // (pn[t], pn[t+1]) as two i16 halves; pn past T is zero
+        const int pp = *reinterpret_cast<const int*>(pn16 + (size_t)j * pstride + t);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) acc[r][i] += pn * (int32_t)(int8_t)(w[i >> 2] >> (8 * (i & 3)));
+        for (int k = 0; k < 8; ++k) {
+          acc[r][2 * k] = __dp2a_lo(pp, (int)x[k], acc[r][2 * k]);
+          acc[r][2 * k + 1] = __dp2a_hi(pp, (int)x[k], acc[r][2 * k + 1]);
+        }
       }
     }
     // lanes holding the same d chunk (same sub) but different keys
@@ -272,30 +322,25 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   }
 }
 
+template <int LPK, int RB>
+static cudaError_t launch_dec_rb(const AttnArgs& a, size_t smem, cudaStream_t st) {
+  const cudaError_t e = launch_k(k_attention_decode<LPK, RB>, dim3(a.B, a.Hkv), dim3(kDecThreads), smem, st, a.q, a.kc,
+                                 a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos, a.Ms, a.Ss, a.Mo, a.So, a.prob_bits,
+                                 a.luts);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+// heads per value pass: up to 4 (register budget of the 16-wide accumulators)
 template <int LPK>
 static cudaError_t launch_dec_l(const AttnArgs& a, size_t smem, cudaStream_t st) {
   const int rep = a.H / a.Hkv;
-  dim3 grid(a.B, a.Hkv);
-  if (rep >= 8) {
-    { const cudaError_t e_ = launch_k(k_attention_decode<LPK, 8>, dim3(grid), dim3(kDecThreads), smem, st, a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos,
-                                                               a.Ms, a.Ss, a.Mo, a.So, a.prob_bits, a.luts); if (e_ != cudaSuccess) return e_; }
-  } else if (rep >= 4) {
-    { const cudaError_t e_ = launch_k(k_attention_decode<LPK, 4>, dim3(grid), dim3(kDecThreads), smem, st, a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos,
-                                                               a.Ms, a.Ss, a.Mo, a.So, a.prob_bits, a.luts); if (e_ != cudaSuccess) return e_; }
-  } else if (rep >= 2) {
-    { const cudaError_t e_ = launch_k(k_attention_decode<LPK, 2>, dim3(grid), dim3(kDecThreads), smem, st, a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos,
-                                                               a.Ms, a.Ss, a.Mo, a.So, a.prob_bits, a.luts); if (e_ != cudaSuccess) return e_; }
-  } else {
-    { const cudaError_t e_ = launch_k(k_attention_decode<LPK, 1>, dim3(grid), dim3(kDecThreads), smem, st, a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos,
-                                                               a.Ms, a.Ss, a.Mo, a.So, a.prob_bits, a.luts); if (e_ != cudaSuccess) return e_; }
-  }
-  return cudaGetLastError();
+  if (rep >= 4) return launch_dec_rb<LPK, 4>(a, smem, st);
+  if (rep >= 2) return launch_dec_rb<LPK, 2>(a, smem, st);
+  return launch_dec_rb<LPK, 1>(a, smem, st);
 }
-
 template <int LPK>
 static cudaError_t prep_dec_l(size_t smem) {
-  for (auto f : {k_attention_decode<LPK, 1>, k_attention_decode<LPK, 2>, k_attention_decode<LPK, 4>,
-                 k_attention_decode<LPK, 8>}) {
+  for (auto f : {k_attention_decode<LPK, 1>, k_attention_decode<LPK, 2>, k_attention_decode<LPK, 4>}) {
     const cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
@@ -314,6 +359,7 @@ cudaError_t prepare_attention(size_t smem) {
 
 cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t st) {
   if (a.B <= 0) return cudaSuccess;
+  if (a.H / a.Hkv > 16) return cudaErrorInvalidValue;
   const size_t smem = attention_decode_smem_bytes(a.H, a.Hkv, a.D, a.max_seq);
   switch (a.D) {
     case 16: return launch_dec_l<1>(a, smem, st);
@@ -328,7 +374,7 @@ cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t st) {
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st) {
   const int R = a.B * a.M;
   if (R <= 0) return cudaSuccess;
-  if (a.M == 1 && (a.D == 16 || a.D == 32 || a.D == 64 || a.D == 128 || a.D == 256))
+  if (a.M == 1 && (a.D == 16 || a.D == 32 || a.D == 64 || a.D == 128 || a.D == 256) && a.H / a.Hkv <= 16)
     return launch_attention_decode(a, st);
   const size_t smem = attention_smem_bytes(a.H, a.Hkv, a.D, a.max_seq);
   dim3 grid(R, a.Hkv);
