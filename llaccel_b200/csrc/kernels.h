@@ -130,6 +130,7 @@ struct AttnArgs {
   int Ss, So;
   int prob_bits;
   const uint16_t* luts;  // device tables (exp LUTs)
+  int32_t* err;          // device error word (a bounded wait timed out)
 };
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st);
 // opt the attention kernel into `smem` bytes of dynamic shared memory (once per device, before capture)

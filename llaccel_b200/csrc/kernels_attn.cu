@@ -131,12 +131,15 @@ __global__ void k_attention(const int8_t* __restrict__ q, const int8_t* __restri
 // ---------------------------------------------------------------------------------------
 constexpr int kDecThreads = 256, kDecWarps = kDecThreads / 32;
 
+// KV tiles stream through a ring of kRing shared-memory stages by 1-D bulk copies.
+constexpr int kRing = 4;
+__host__ __device__ constexpr int dec_tile_keys(int D) { return D <= 64 ? 256 : 16384 / D; }
+
 size_t attention_decode_smem_bytes(int H, int Hkv, int D, int max_seq) {
   const int rep = H / Hkv;
-  // scores / probabilities (i32), normalised probabilities (i16), per-warp partial sums of
-  // the value pass, q rows, per-warp head maxima and sums
-  return (size_t)rep * D + (size_t)rep * max_seq * 4 + (size_t)rep * (size_t)((max_seq + 3) & ~1) * 2 +
-         (size_t)kDecWarps * rep * D * 4 + (size_t)kDecWarps * rep * 8 + 64;
+  const size_t ring = (size_t)kRing * dec_tile_keys(D) * D;
+  return ring + (size_t)rep * D + (size_t)rep * max_seq * 4 + (size_t)rep * (size_t)((max_seq + 3) & ~1) * 2 +
+         (size_t)kDecWarps * rep * D * 4 + (size_t)kDecWarps * rep * 8 + 128;
 }
 
 __device__ __forceinline__ int dot16_i8(const uint4& a, const uint4& b, int acc) {
@@ -147,18 +150,49 @@ __device__ __forceinline__ int dot16_i8(const uint4& a, const uint4& b, int acc)
   return acc;
 }
 
+__device__ __forceinline__ uint32_t att_smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void att_mbar_init(uint64_t* bar) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(att_smem_u32(bar)));
+}
+__device__ __forceinline__ void att_bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(att_smem_u32(bar)), "r"(bytes) : "memory");
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   att_smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(att_smem_u32(bar))
+               : "memory");
+}
+// bounded wait on an mbarrier phase: false after ~2^26 polls
+__device__ __forceinline__ bool att_mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < (1u << 26); ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(att_smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
 template <int LPK, int RB>
 __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
     const int8_t* __restrict__ q, const int8_t* __restrict__ kc, const int8_t* __restrict__ vc, int8_t* __restrict__ out,
     int H, int Hkv, int max_seq, const int* __restrict__ d_pos, int64_t Ms, int Ss, int64_t Mo, int So, int prob_bits,
-    const uint16_t* __restrict__ luts) {
+    const uint16_t* __restrict__ luts, int32_t* err) {
   constexpr int D = LPK * 16;
   constexpr int KPW = 32 / LPK;  // key rows per warp per step
-  extern __shared__ __align__(16) unsigned char smem[];
+  constexpr int TK = dec_tile_keys(D);
+  extern __shared__ __align__(128) unsigned char smem[];
   __shared__ uint16_t s_expi[16], s_expf[256];
+  __shared__ __align__(8) uint64_t full_bar[kRing];
+  __shared__ int s_abort;
   const int rep = H / Hkv;
-  const int pstride = (max_seq + 3) & ~1;                                // i16 row stride (even, > max_seq)
-  int8_t* q_s = reinterpret_cast<int8_t*>(smem);                         // [rep][D] (16-byte rows)
+  const int pstride = (max_seq + 3) & ~1;
+  int8_t* ring = reinterpret_cast<int8_t*>(smem);                        // [kRing][TK][D]
+  int8_t* q_s = ring + (size_t)kRing * TK * D;                           // [rep][D]
   int32_t* sc = reinterpret_cast<int32_t*>(q_s + rep * D);               // [rep][max_seq] scores, then p
   int16_t* pn16 = reinterpret_cast<int16_t*>(sc + (size_t)rep * max_seq);  // [rep][pstride] normalised p
   int32_t* red = reinterpret_cast<int32_t*>(pn16 + (size_t)rep * pstride);  // [warps][rep][D]
@@ -167,6 +201,11 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   const int b = blockIdx.x, kvh = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane % LPK, kg = lane / LPK;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kRing; ++i) att_mbar_init(&full_bar[i]);
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
   pdl_trigger();
   for (int i = threadIdx.x; i < 16 + 256; i += blockDim.x) {
     if (i < 16)
@@ -176,124 +215,155 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   }
   pdl_wait();  // POS, q and the KV cache come from earlier kernels
   const int T = *d_pos + 1;
+  const int ntile = (T + TK - 1) / TK;  // tiles of K, then as many of V
+  const int8_t* kbase = kc + ((int64_t)b * Hkv + kvh) * max_seq * D;
+  const int8_t* vbase = vc + ((int64_t)b * Hkv + kvh) * max_seq * D;
+  auto issue = [&](int i) {  // tile i of the K-then-V sequence into stage i % kRing
+    const int kv = i >= ntile, ti = kv ? i - ntile : i;
+    const int t0 = ti * TK, nk = min(TK, T - t0);
+    att_bulk_load(ring + (size_t)(i % kRing) * TK * D, (kv ? vbase : kbase) + (int64_t)t0 * D, (uint32_t)(nk * D),
+                  &full_bar[i % kRing]);
+  };
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int i = 0; i < min(kRing, 2 * ntile); ++i) issue(i);
   const int8_t* qrow = q + ((int64_t)b * H + (int64_t)kvh * rep) * D;
   for (int i = threadIdx.x; i < rep * D / 16; i += blockDim.x)
     reinterpret_cast<uint4*>(q_s)[i] = reinterpret_cast<const uint4*>(qrow)[i];
-  __syncthreads();
 
-  const int8_t* kbase = kc + ((int64_t)b * Hkv + kvh) * max_seq * D;
-  const int8_t* vbase = vc + ((int64_t)b * Hkv + kvh) * max_seq * D;
-  const int stride = kDecWarps * KPW;
-
-  // ---- scores, with each head's running maximum ----
   int32_t mxl[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) mxl[j] = INT_MIN;
-  for (int t0 = warp * KPW; t0 < T; t0 += 2 * stride) {
-    const int ta = t0 + kg, tb = t0 + stride + kg;
-    uint4 ka = make_uint4(0, 0, 0, 0), kb = make_uint4(0, 0, 0, 0);
-    if (ta < T) ka = __ldg(reinterpret_cast<const uint4*>(kbase + (int64_t)ta * D) + sub);
-    if (tb < T) kb = __ldg(reinterpret_cast<const uint4*>(kbase + (int64_t)tb * D) + sub);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      if (j >= rep) break;
-      const uint4 qv = reinterpret_cast<const uint4*>(q_s + j * D)[sub];
-      int sa = dot16_i8(ka, qv, 0), sb = dot16_i8(kb, qv, 0);
-#pragma unroll
-      for (int o = 1; o < LPK; o <<= 1) {
-        sa += __shfl_xor_sync(0xffffffffu, sa, o);
-        sb += __shfl_xor_sync(0xffffffffu, sb, o);
-      }
-      if (ta < T) {
-        mxl[j] = max(mxl[j], sa);
-        if (sub == 0) sc[j * max_seq + ta] = sa;
-      }
-      if (tb < T) {
-        mxl[j] = max(mxl[j], sb);
-        if (sub == 0) sc[j * max_seq + tb] = sb;
-      }
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    if (j >= rep) break;
-    int32_t v = mxl[j];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
-    if (lane == 0) wmax[warp * rep + j] = v;
-  }
-  __syncthreads();
-
-  // ---- exp LUT probabilities and their sums (all threads, heads outer) ----
   const int pmax = (1 << prob_bits) - 1, pshift = 31 - prob_bits;
-  for (int j = 0; j < rep; ++j) {
-    int32_t mx = wmax[j];
-    for (int w = 1; w < kDecWarps; ++w) mx = max(mx, wmax[w * rep + j]);
-    int32_t* s = sc + j * max_seq;
-    uint32_t sum = 0;
-    for (int t = threadIdx.x; t < T; t += blockDim.x) {
-      const uint32_t p = exp_prob(mulshift((int64_t)mx - s[t], Ms, Ss), s_expi, s_expf);
-      s[t] = (int32_t)p;
-      sum += p;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane == 0) wsum[warp * rep + j] = sum;
-  }
-  __syncthreads();
-  // ---- normalised probabilities (Q0.15 or Q0.8) as i16, zero past the last key ----
-  for (int j = 0; j < rep; ++j) {
-    uint32_t sum = 0;
-    for (int w = 0; w < kDecWarps; ++w) sum += wsum[w * rep + j];
-    const int64_t inv = udiv((uint64_t)1 << 31, sum);
-    const int32_t* s = sc + j * max_seq;
-    int16_t* pj = pn16 + (size_t)j * pstride;
-    for (int t = threadIdx.x; t < T + 2; t += blockDim.x) {
-      int32_t v = 0;
-      if (t < T) {
-        const int64_t pn = rshr((int64_t)s[t] * inv, pshift);
-        v = (int32_t)(pn < pmax ? pn : pmax);
-      }
-      if (t < pstride) pj[t] = (int16_t)v;
-    }
-  }
-  __syncthreads();
-
-  // ---- o[j][d] = sum_t pn[j][t] * v[t][d]: key pairs through dp2a, RB heads per pass ----
+  int32_t acc[RB][16];
   int8_t* orow = out + ((int64_t)b * H + (int64_t)kvh * rep) * D;
-  const int pair_stride = kDecWarps * KPW * 2;
+  // heads j0..j0+RB-1 accumulate per V pass; rep > RB re-streams V (rare: tiles stay in L2)
   for (int j0 = 0; j0 < rep; j0 += RB) {
-    int32_t acc[RB][16];
 #pragma unroll
     for (int r = 0; r < RB; ++r)
 #pragma unroll
       for (int i = 0; i < 16; ++i) acc[r][i] = 0;
-    for (int t = (warp * KPW + kg) * 2; t < T; t += pair_stride) {
-      const uint4 va = __ldg(reinterpret_cast<const uint4*>(vbase + (int64_t)t * D) + sub);
-      uint4 vb = make_uint4(0, 0, 0, 0);
-      if (t + 1 < T) vb = __ldg(reinterpret_cast<const uint4*>(vbase + (int64_t)(t + 1) * D) + sub);
-      // (v_t[d], v_t+1[d]) byte pairs: x[2k] holds d = 4k, 4k+1; x[2k+1] holds d = 4k+2, 4k+3
-      const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
-      uint32_t x[8];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        x[2 * k] = __byte_perm(wa[k], wb[k], 0x5140);
-        x[2 * k + 1] = __byte_perm(wa[k], wb[k], 0x7362);
+    const int first = j0 == 0 ? 0 : ntile;  // later head groups only need the V tiles again
+    if (j0 > 0) {
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        // restart the ring on the V tiles: re-initialise the stage barriers (all idle here)
+        for (int i = 0; i < kRing; ++i) {
+          asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(att_smem_u32(&full_bar[i])));
+          att_mbar_init(&full_bar[i]);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
       }
+      __syncthreads();
+      if (threadIdx.x == 0)
+        for (int i = ntile; i < min(ntile + kRing, 2 * ntile); ++i) issue(i);
+    }
+    for (int i = first; i < 2 * ntile; ++i) {
+      const int stage = i % kRing;
+      const uint32_t parity = (uint32_t)(((j0 == 0 ? i : i - ntile) / kRing) & 1);
+      if (!att_mbar_wait(&full_bar[stage], parity)) {
+        s_abort = 1;
+        if (err) atomicExch(err, 5);
+      }
+      __syncthreads();
+      if (s_abort) break;
+      const int8_t* tile = ring + (size_t)stage * TK * D;
+      const int kv = i >= ntile, ti = kv ? i - ntile : i;
+      const int t0 = ti * TK, nk = min(TK, T - t0);
+      if (!kv) {
+        // ---- scores of this K tile, running per-head maxima ----
+        // uniform trip count per warp: the shuffles below need every lane
+        for (int base = 0; base < nk; base += KPW * kDecWarps) {
+          const int l = base + warp * KPW + kg;
+          const bool ok = l < nk;
+          const uint4 kk = ok ? reinterpret_cast<const uint4*>(tile + (size_t)l * D)[sub] : make_uint4(0, 0, 0, 0);
 #pragma unroll
-      for (int r = 0; r < RB; ++r) {
-        const int j = j0 + r;
-        if (j >= rep) break;
-        // (pn[t], pn[t+1]) as two i16 halves; pn past T is zero
-        const int pp = *reinterpret_cast<const int*>(pn16 + (size_t)j * pstride + t);
+          for (int j = 0; j < 16; ++j) {
+            if (j >= rep) break;
+            const uint4 qv = reinterpret_cast<const uint4*>(q_s + j * D)[sub];
+            int sv = dot16_i8(kk, qv, 0);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          acc[r][2 * k] = __dp2a_lo(pp, (int)x[k], acc[r][2 * k]);
-          acc[r][2 * k + 1] = __dp2a_hi(pp, (int)x[k], acc[r][2 * k + 1]);
+            for (int o = 1; o < LPK; o <<= 1) sv += __shfl_xor_sync(0xffffffffu, sv, o);
+            if (ok) {
+              mxl[j] = max(mxl[j], sv);
+              if (sub == 0) sc[j * max_seq + t0 + l] = sv;
+            }
+          }
+        }
+        if (i == ntile - 1) {
+          // ---- all scores are in: per-head max, exp LUT probabilities, sums, Q0.15 ----
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            if (j >= rep) break;
+            int32_t v = mxl[j];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+            if (lane == 0) wmax[warp * rep + j] = v;
+          }
+          __syncthreads();
+          for (int j = 0; j < rep; ++j) {
+            int32_t mx = wmax[j];
+            for (int w = 1; w < kDecWarps; ++w) mx = max(mx, wmax[w * rep + j]);
+            int32_t* sj = sc + j * max_seq;
+            uint32_t sum = 0;
+            for (int t = threadIdx.x; t < T; t += blockDim.x) {
+              const uint32_t p = exp_prob(mulshift((int64_t)mx - sj[t], Ms, Ss), s_expi, s_expf);
+              sj[t] = (int32_t)p;
+              sum += p;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (lane == 0) wsum[warp * rep + j] = sum;
+          }
+          __syncthreads();
+          for (int j = 0; j < rep; ++j) {
+            uint32_t sum = 0;
+            for (int w = 0; w < kDecWarps; ++w) sum += wsum[w * rep + j];
+            const int64_t inv = udiv((uint64_t)1 << 31, sum);
+            const int32_t* sj = sc + j * max_seq;
+            int16_t* pj = pn16 + (size_t)j * pstride;
+            for (int t = threadIdx.x; t < T + 2; t += blockDim.x) {
+              int32_t v = 0;
+              if (t < T) {
+                const int64_t pn = rshr((int64_t)sj[t] * inv, pshift);
+                v = (int32_t)(pn < pmax ? pn : pmax);
+              }
+              if (t < pstride) pj[t] = (int16_t)v;
+            }
+          }
+        }
+      } else {
+        // ---- values of this V tile: key pairs through dp2a ----
+        for (int l = (warp * KPW + kg) * 2; l < nk; l += KPW * kDecWarps * 2) {
+          const int t = t0 + l;
+          const uint4 va = reinterpret_cast<const uint4*>(tile + (size_t)l * D)[sub];
+          // the row after the last key is stale shared memory, weighted by pn = 0
+          const uint4 vb = reinterpret_cast<const uint4*>(tile + (size_t)(l + 1) * D)[sub];
+          const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
+          uint32_t x[8];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            x[2 * k] = __byte_perm(wa[k], wb[k], 0x5140);
+            x[2 * k + 1] = __byte_perm(wa[k], wb[k], 0x7362);
+          }
+#pragma unroll
+          for (int r = 0; r < RB; ++r) {
+            const int j = j0 + r;
+            if (j >= rep) break;
+            const int pp = *reinterpret_cast<const int*>(pn16 + (size_t)j * pstride + t);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              acc[r][2 * k] = __dp2a_lo(pp, (int)x[k], acc[r][2 * k]);
+              acc[r][2 * k + 1] = __dp2a_hi(pp, (int)x[k], acc[r][2 * k + 1]);
+            }
+          }
         }
       }
+      __syncthreads();  // stage consumed by every thread
+      if (threadIdx.x == 0 && i + kRing < 2 * ntile) issue(i + kRing);
     }
-    // lanes holding the same d chunk (same sub) but different keys
+    if (s_abort) break;
+    // ---- reduce the value sums: lanes with the same d chunk, then warps ----
 #pragma unroll
     for (int o = LPK; o < 32; o <<= 1)
 #pragma unroll
@@ -318,15 +388,30 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
       if (prob_bits == 15) ov = rshr(ov, 7);
       orow[j * D + d] = (int8_t)sat8(mulshift(ov, Mo, So));
     }
-    __syncthreads();
   }
+  // drain (bounded) the copies still in flight after an abort before the CTA exits
+  __syncthreads();
+  if (threadIdx.x == 0 && s_abort)
+    for (int i = 0; i < kRing; ++i) {
+      for (uint32_t it = 0; it < (1u << 20); ++it) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(att_smem_u32(&full_bar[i])), "r"(0u)
+            : "memory");
+        if (ok) break;
+      }
+    }
 }
 
 template <int LPK, int RB>
 static cudaError_t launch_dec_rb(const AttnArgs& a, size_t smem, cudaStream_t st) {
   const cudaError_t e = launch_k(k_attention_decode<LPK, RB>, dim3(a.B, a.Hkv), dim3(kDecThreads), smem, st, a.q, a.kc,
                                  a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos, a.Ms, a.Ss, a.Mo, a.So, a.prob_bits,
-                                 a.luts);
+                                 a.luts, a.err);
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 

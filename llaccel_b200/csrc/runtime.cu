@@ -975,6 +975,7 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
         a.So = x.So;
         a.prob_bits = x.prob_bits;
         a.luts = m->d_luts;
+        a.err = s->d_fault;
         e = launch_attention(a, st);
         break;
       }
