@@ -135,8 +135,11 @@ constexpr int kDecThreads = 256, kDecWarps = kDecThreads / 32;
 constexpr int kRing = 4;
 __host__ __device__ constexpr int dec_tile_keys(int D) { return D <= 64 ? 256 : 16384 / D; }
 
+// heads per CTA: a KV head's H/Hkv query heads are split into groups of at most 4
+__host__ __device__ constexpr int dec_heads_per_cta(int rep) { return rep < 4 ? rep : 4; }
+
 size_t attention_decode_smem_bytes(int H, int Hkv, int D, int max_seq) {
-  const int rep = H / Hkv;
+  const int rep = dec_heads_per_cta(H / Hkv);
   const size_t ring = (size_t)kRing * dec_tile_keys(D) * D;
   return ring + (size_t)rep * D + (size_t)rep * max_seq * 4 + (size_t)rep * (size_t)((max_seq + 3) & ~1) * 2 +
          (size_t)kDecWarps * rep * D * 4 + (size_t)kDecWarps * rep * 8 + 128;
@@ -189,7 +192,10 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   __shared__ uint16_t s_expi[16], s_expf[256];
   __shared__ __align__(8) uint64_t full_bar[kRing];
   __shared__ int s_abort;
-  const int rep = H / Hkv;
+  // this CTA serves query heads [h0, h0 + rep) of KV head blockIdx.y
+  const int rep_all = H / Hkv;
+  const int hg0 = blockIdx.z * RB;
+  const int rep = min(RB, rep_all - hg0);
   const int pstride = (max_seq + 3) & ~1;
   int8_t* ring = reinterpret_cast<int8_t*>(smem);                        // [kRing][TK][D]
   int8_t* q_s = ring + (size_t)kRing * TK * D;                           // [rep][D]
@@ -227,7 +233,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   __syncthreads();
   if (threadIdx.x == 0)
     for (int i = 0; i < min(kRing, 2 * ntile); ++i) issue(i);
-  const int8_t* qrow = q + ((int64_t)b * H + (int64_t)kvh * rep) * D;
+  const int8_t* qrow = q + ((int64_t)b * H + (int64_t)kvh * rep_all + hg0) * D;
   for (int i = threadIdx.x; i < rep * D / 16; i += blockDim.x)
     reinterpret_cast<uint4*>(q_s)[i] = reinterpret_cast<const uint4*>(qrow)[i];
 
@@ -236,31 +242,16 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   for (int j = 0; j < 16; ++j) mxl[j] = INT_MIN;
   const int pmax = (1 << prob_bits) - 1, pshift = 31 - prob_bits;
   int32_t acc[RB][16];
-  int8_t* orow = out + ((int64_t)b * H + (int64_t)kvh * rep) * D;
-  // heads j0..j0+RB-1 accumulate per V pass; rep > RB re-streams V (rare: tiles stay in L2)
-  for (int j0 = 0; j0 < rep; j0 += RB) {
+  int8_t* orow = out + ((int64_t)b * H + (int64_t)kvh * rep_all + hg0) * D;
+  {
+    const int j0 = 0;  // rep <= RB: every head of this CTA in one pass over V
 #pragma unroll
     for (int r = 0; r < RB; ++r)
 #pragma unroll
       for (int i = 0; i < 16; ++i) acc[r][i] = 0;
-    const int first = j0 == 0 ? 0 : ntile;  // later head groups only need the V tiles again
-    if (j0 > 0) {
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        // restart the ring on the V tiles: re-initialise the stage barriers (all idle here)
-        for (int i = 0; i < kRing; ++i) {
-          asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(att_smem_u32(&full_bar[i])));
-          att_mbar_init(&full_bar[i]);
-        }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-      }
-      __syncthreads();
-      if (threadIdx.x == 0)
-        for (int i = ntile; i < min(ntile + kRing, 2 * ntile); ++i) issue(i);
-    }
-    for (int i = first; i < 2 * ntile; ++i) {
+    for (int i = 0; i < 2 * ntile; ++i) {
       const int stage = i % kRing;
-      const uint32_t parity = (uint32_t)(((j0 == 0 ? i : i - ntile) / kRing) & 1);
+      const uint32_t parity = (uint32_t)((i / kRing) & 1);
       if (!att_mbar_wait(&full_bar[stage], parity)) {
         s_abort = 1;
         if (err) atomicExch(err, 5);
@@ -362,7 +353,9 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
       __syncthreads();  // stage consumed by every thread
       if (threadIdx.x == 0 && i + kRing < 2 * ntile) issue(i + kRing);
     }
-    if (s_abort) break;
+  }
+  if (!s_abort) {
+    const int j0 = 0;
     // ---- reduce the value sums: lanes with the same d chunk, then warps ----
 #pragma unroll
     for (int o = LPK; o < 32; o <<= 1)
@@ -409,13 +402,14 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
 
 template <int LPK, int RB>
 static cudaError_t launch_dec_rb(const AttnArgs& a, size_t smem, cudaStream_t st) {
-  const cudaError_t e = launch_k(k_attention_decode<LPK, RB>, dim3(a.B, a.Hkv), dim3(kDecThreads), smem, st, a.q, a.kc,
+  const int groups = (a.H / a.Hkv + RB - 1) / RB;
+  const cudaError_t e = launch_k(k_attention_decode<LPK, RB>, dim3(a.B, a.Hkv, groups), dim3(kDecThreads), smem, st, a.q, a.kc,
                                  a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos, a.Ms, a.Ss, a.Mo, a.So, a.prob_bits,
                                  a.luts, a.err);
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
-// heads per value pass: up to 4 (register budget of the 16-wide accumulators)
+// heads per CTA (and per value pass): dec_heads_per_cta
 template <int LPK>
 static cudaError_t launch_dec_l(const AttnArgs& a, size_t smem, cudaStream_t st) {
   const int rep = a.H / a.Hkv;
@@ -444,7 +438,7 @@ cudaError_t prepare_attention(size_t smem) {
 
 cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t st) {
   if (a.B <= 0) return cudaSuccess;
-  if (a.H / a.Hkv > 16) return cudaErrorInvalidValue;
+
   const size_t smem = attention_decode_smem_bytes(a.H, a.Hkv, a.D, a.max_seq);
   switch (a.D) {
     case 16: return launch_dec_l<1>(a, smem, st);
@@ -459,7 +453,7 @@ cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t st) {
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st) {
   const int R = a.B * a.M;
   if (R <= 0) return cudaSuccess;
-  if (a.M == 1 && (a.D == 16 || a.D == 32 || a.D == 64 || a.D == 128 || a.D == 256) && a.H / a.Hkv <= 16)
+  if (a.M == 1 && (a.D == 16 || a.D == 32 || a.D == 64 || a.D == 128 || a.D == 256))
     return launch_attention_decode(a, st);
   const size_t smem = attention_smem_bytes(a.H, a.Hkv, a.D, a.max_seq);
   dim3 grid(R, a.Hkv);
