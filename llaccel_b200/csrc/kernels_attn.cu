@@ -154,6 +154,16 @@ __device__ __forceinline__ int dot16_i8(const uint4& a, const uint4& b, int acc)
 }
 
 __device__ __forceinline__ uint32_t att_smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// exp-LUT probability of a score gap d = mx - s >= 0 (numerics.h:104-107): z = rshr(d * Ms, Ss)
+// with d < 2^31 and Ms < 2^32, so one u32 x u32 -> u64 product carries it exactly
+__device__ __forceinline__ uint32_t gap_prob(uint32_t d, uint32_t Ms, int Ss, const uint16_t* expi, const uint16_t* expf) {
+  const uint64_t prod = (uint64_t)d * Ms;
+  const uint64_t z = Ss == 0 ? prod : (prod >> Ss) + ((prod >> (Ss - 1)) & 1ull);
+  if (z >= 4096u) return 0;
+  const uint32_t zi = (uint32_t)z;
+  return ((uint32_t)expi[zi >> 8] * (uint32_t)expf[zi & 255] + (1u << 15)) >> 16;
+}
 __device__ __forceinline__ void att_mbar_init(uint64_t* bar) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(att_smem_u32(bar)));
 }
@@ -192,6 +202,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   __shared__ uint16_t s_expi[16], s_expf[256];
   __shared__ __align__(8) uint64_t full_bar[kRing];
   __shared__ int s_abort;
+  __shared__ uint32_t s_inv[16];
   // this CTA serves query heads [h0, h0 + rep) of KV head blockIdx.y
   const int rep_all = H / Hkv;
   const int hg0 = blockIdx.z * RB;
@@ -262,22 +273,28 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
       const int kv = i >= ntile, ti = kv ? i - ntile : i;
       const int t0 = ti * TK, nk = min(TK, T - t0);
       if (!kv) {
-        // ---- scores of this K tile, running per-head maxima ----
-        // uniform trip count per warp: the shuffles below need every lane
-        for (int base = 0; base < nk; base += KPW * kDecWarps) {
-          const int l = base + warp * KPW + kg;
-          const bool ok = l < nk;
-          const uint4 kk = ok ? reinterpret_cast<const uint4*>(tile + (size_t)l * D)[sub] : make_uint4(0, 0, 0, 0);
+        // ---- scores of this K tile (one key per lane), running per-head maxima ----
+        // lane l reads its row's 16-byte chunks starting at chunk l % LPK, so the 32 rows of a
+        // warp spread over all shared-memory banks
+        for (int l = warp * 32 + lane; l < nk; l += 32 * kDecWarps) {
+          const int8_t* krow = tile + (size_t)l * D;
+          int sv[RB];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            if (j >= rep) break;
-            const uint4 qv = reinterpret_cast<const uint4*>(q_s + j * D)[sub];
-            int sv = dot16_i8(kk, qv, 0);
+          for (int r = 0; r < RB; ++r) sv[r] = 0;
 #pragma unroll
-            for (int o = 1; o < LPK; o <<= 1) sv += __shfl_xor_sync(0xffffffffu, sv, o);
-            if (ok) {
-              mxl[j] = max(mxl[j], sv);
-              if (sub == 0) sc[j * max_seq + t0 + l] = sv;
+          for (int cc = 0; cc < LPK; ++cc) {
+            const int c = (cc + l) % LPK;
+            const uint4 kk = reinterpret_cast<const uint4*>(krow)[c];
+#pragma unroll
+            for (int r = 0; r < RB; ++r) {
+              if (r < rep) sv[r] = dot16_i8(kk, reinterpret_cast<const uint4*>(q_s + r * D)[c], sv[r]);
+            }
+          }
+#pragma unroll
+          for (int r = 0; r < RB; ++r) {
+            if (r < rep) {
+              mxl[r] = max(mxl[r], sv[r]);
+              sc[r * max_seq + t0 + l] = sv[r];
             }
           }
         }
@@ -298,7 +315,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
             int32_t* sj = sc + j * max_seq;
             uint32_t sum = 0;
             for (int t = threadIdx.x; t < T; t += blockDim.x) {
-              const uint32_t p = exp_prob(mulshift((int64_t)mx - sj[t], Ms, Ss), s_expi, s_expf);
+              const uint32_t p = gap_prob((uint32_t)(mx - sj[t]), (uint32_t)Ms, Ss, s_expi, s_expf);
               sj[t] = (int32_t)p;
               sum += p;
             }
@@ -307,17 +324,24 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
             if (lane == 0) wsum[warp * rep + j] = sum;
           }
           __syncthreads();
-          for (int j = 0; j < rep; ++j) {
+          if (threadIdx.x < rep) {
+            // inv = udiv(2^31, sum): 2^31 fits 32 bits, so a 32-bit divide is exact
             uint32_t sum = 0;
-            for (int w = 0; w < kDecWarps; ++w) sum += wsum[w * rep + j];
-            const int64_t inv = udiv((uint64_t)1 << 31, sum);
+            for (int w = 0; w < kDecWarps; ++w) sum += wsum[w * rep + threadIdx.x];
+            s_inv[threadIdx.x] = 0x80000000u / (sum ? sum : 1u);
+          }
+          __syncthreads();
+          for (int j = 0; j < rep; ++j) {
+            // p <= sum, so p * inv <= 2^31 - 1: the product and its rounding shift stay in 32 bits
+            const uint32_t inv = s_inv[j];
             const int32_t* sj = sc + j * max_seq;
             int16_t* pj = pn16 + (size_t)j * pstride;
             for (int t = threadIdx.x; t < T + 2; t += blockDim.x) {
               int32_t v = 0;
               if (t < T) {
-                const int64_t pn = rshr((int64_t)sj[t] * inv, pshift);
-                v = (int32_t)(pn < pmax ? pn : pmax);
+                const uint32_t x = (uint32_t)sj[t] * inv;
+                const uint32_t pn = (x >> pshift) + ((x >> (pshift - 1)) & 1u);
+                v = (int32_t)(pn < (uint32_t)pmax ? pn : (uint32_t)pmax);
               }
               if (t < pstride) pj[t] = (int16_t)v;
             }
