@@ -63,10 +63,14 @@ def parse_args():
 # distributed plumbing
 # ---------------------------------------------------------------------------------------
 class Dist:
-    def __init__(self, want: int) -> None:
+    """One process per GPU (torchrun env): barrier and max-over-ranks timing.  backend
+    "nccl" on GPUs; "gloo" serves the CPU tests of the same plumbing."""
+
+    def __init__(self, want: int, backend: str = "nccl") -> None:
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.backend = backend
         self.pg = None
         if self.world > 1:
             import datetime
@@ -74,9 +78,11 @@ class Dist:
             import torch
             import torch.distributed as dist
 
-            torch.cuda.set_device(self.local)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                    device_id=torch.device("cuda", self.local))
+            kw = {}
+            if backend == "nccl":
+                torch.cuda.set_device(self.local)
+                kw["device_id"] = torch.device("cuda", self.local)
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600), **kw)
             self.pg = dist
         if want != self.world and self.world > 1:
             raise SystemExit(f"--gpus {want} but WORLD_SIZE {self.world}")
@@ -89,13 +95,14 @@ class Dist:
         if not self.pg:
             return x
         import torch
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        t = torch.tensor([x], dtype=torch.float64, device="cuda" if self.backend == "nccl" else "cpu")
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
     def close(self) -> None:
         if self.pg:
             self.pg.destroy_process_group()
+            self.pg = None
 
 
 # ---------------------------------------------------------------------------------------
