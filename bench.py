@@ -293,6 +293,40 @@ def _by_kind(prof: list[dict]) -> dict:
             for k, v in sorted(out.items(), key=lambda kv: -kv[1][1])}
 
 
+# plan step kind -> the kernel function that executes it on the decode path (M = 1 row per
+# sequence, B >= 16 rows: tensor-core GEMMs)
+_KERNEL_OF = {"linear": "k_linear_tc", "linear_group": "k_linear_tc", "gated": "k_linear_tc",
+              "linear_partial": "k_linear_tc", "attention": "k_attention_decode", "rmsnorm": "k_rmsnorm",
+              "rope_group": "k_rope_group", "rope": "k_rope", "add": "k_add", "mul": "k_mul", "silu": "k_silu",
+              "quant": "k_quant", "kv_write": "k_kv_write", "embed": "k_embed", "argmax": "k_amax_finish",
+              "requant": "k_requant", "allreduce": "ncclAllReduce"}
+
+
+def _by_kernel(prof: list[dict]) -> dict:
+    """Per-kernel-function totals of one decode launch: launches, ms, algorithmic bytes."""
+    out: dict[str, dict] = {}
+    for p in prof:
+        kind = p["label"].partition(":")[0]
+        k = _KERNEL_OF.get(kind, kind)
+        e = out.setdefault(k, {"n": 0, "ms": 0.0, "bytes": 0.0})
+        e["n"] += 1
+        e["ms"] += p["ms"]
+        e["bytes"] += p["bytes"]
+    return out
+
+
+def _committed_traffic(config: str, batch: int, kernel: str):
+    """DRAM traffic per launch of `kernel` from a committed ncu summary, if one exists for
+    this config and batch (profiles/traffic.json, written from an ncu capture)."""
+    f = REPO / "profiles" / "traffic.json"
+    if not f.exists():
+        return None
+    for e in json.loads(f.read_text()).get("entries", []):
+        if e.get("config") == config and e.get("batch") == batch and e.get("kernel") == kernel:
+            return e
+    return None
+
+
 def run_ours(args, dist: Dist) -> None:
     import torch
     from llaccel_b200 import build
@@ -401,17 +435,30 @@ def run_ours(args, dist: Dist) -> None:
     prof = m0.profile_decode(pos_mid, iters=20)
     launches_per_step = m0.decode_launches_per_step()
     step_ms_sum = sum(p["ms"] for p in prof)
-    dom = max(prof, key=lambda p: p["ms"])
+    kern = _by_kernel(prof)
+    dom_name = max(kern, key=lambda k: kern[k]["ms"])
+    dom = kern[dom_name]
     peaks = {}
     pk = REPO / "MEASURED_PEAKS.json"
     if pk.exists():
         peaks = json.loads(pk.read_text())
     hbm = float(peaks.get("hbm_gbs", 6650.0))
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    # the dominant kernel = the kernel function with the largest share of the decode launch;
+    # achieved = its algorithmic bytes per launch / its average launch duration (CUDA events)
     dom_gbs = dom["bytes"] / (dom["ms"] / 1e3) / 1e9
-    roof = {"bound": "hbm", "kernel": dom["label"], "achieved": dom_gbs, "peak": hbm, "unit": "GB/s",
-            "frac": dom_gbs / hbm, "peak_source": peak_src, "traffic": None,
-            "bytes_per_launch": dom["bytes"], "ms_per_launch": dom["ms"], "share_of_step": dom["ms"] / step_ms_sum}
+    traffic = _committed_traffic(cfg.name, B, dom_name)
+    roof = {"bound": "hbm", "kernel": dom_name, "achieved": dom_gbs, "peak": hbm, "unit": "GB/s",
+            "frac": dom_gbs / hbm, "peak_source": peak_src,
+            "traffic": traffic["bytes_per_launch"] if traffic else None,
+            "traffic_source": traffic["source"] if traffic else None,
+            "launches_per_decode_launch": dom["n"], "bytes_per_launch": dom["bytes"] / dom["n"],
+            "ms_per_launch": dom["ms"] / dom["n"], "share_of_step": dom["ms"] / step_ms_sum,
+            "by_kernel": {k: {"n": v["n"], "share": round(v["ms"] / step_ms_sum, 4),
+                              "us_per_launch": round(1e3 * v["ms"] / v["n"], 2),
+                              "GBs": round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1),
+                              "frac": round(v["bytes"] / (v["ms"] / 1e3) / 1e9 / hbm, 4)}
+                          for k, v in sorted(kern.items(), key=lambda kv: -kv[1]["ms"])}}
     # whole decode launch (all lanes): algorithmic bytes = weights once per lane + KV + acts
     step_bytes = sum(p["bytes"] for p in prof) * lanes
     step_ms_graph = ms_max / args.steps / n_dec

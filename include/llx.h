@@ -61,6 +61,10 @@ typedef struct {
   int E_RES, E_LOGIT;
   int n_ops, n_steps, n_activations;
   size_t weight_bytes;
+  /* tensor parallelism (1, 0, 0 on one GPU): this rank's graph outputs global vocabulary
+   * channels [vocab_base, vocab_base + vocab_local); vocab_padded is the full width that
+   * logits outputs carry.  n_heads / n_kv_heads are this rank's heads. */
+  int tp_world, tp_rank, vocab_base, vocab_local;
 } llx_model_info;
 
 /* Load qgraph_dir/{qgraph.json, <weights_file>}, validate every op, upload weights,
@@ -128,6 +132,22 @@ llx_status llx_read_activation(llx_session* s, const char* name, void* dst, size
 
 const char* llx_last_error(void);
 const char* llx_version(void);
+
+/* Tensor parallelism over NCCL (NVLink / NVSwitch).  A tensor-parallel group is `world`
+ * processes, one per GPU, each loading its rank graph (written by llaccel_b200.tp.shard:
+ * column-split q/k/v/gate/up/lm_head, row-split o/down as int32 partial sums + all-reduce +
+ * requant).  No counterpart in the reference, which runs one device; results stay bit for
+ * bit those of the unsharded graph.  Rank 0 calls llx_tp_unique_id and shares the 128
+ * bytes with the other ranks (e.g. over torch.distributed); then every rank calls
+ * llx_tp_init on its loaded model (collective: blocks until all ranks joined) before it
+ * creates its one session.  From then on every launch call (llx_run, llx_run_rows,
+ * llx_generate, llx_decode_async, llx_profile_decode) is collective: all ranks make the
+ * same calls with the same shapes, positions and output choices (logits outputs all-gather
+ * the vocabulary shards).  Argmax outputs are global token ids on every rank.  The
+ * communicator lives until llx_model_destroy; NCCL is loaded at run time (libnccl.so.2). */
+#define LLX_TP_UNIQUE_ID_BYTES 128
+llx_status llx_tp_unique_id(void* id);
+llx_status llx_tp_init(llx_model* m, const void* id, int rank, int world);
 
 /* Output projection with fused argmax that allocates no device memory.
  * No counterpart in the reference: it exists for callers that cannot call cudaMalloc --

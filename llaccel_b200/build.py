@@ -68,7 +68,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
             print(r.stdout + r.stderr)
         objs.append(str(obj))
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *ARCH_FLAGS, "-shared", "-o", str(tmp), *objs, "-lcuda"]
+    cmd = [nvcc(), *ARCH_FLAGS, "-shared", "-o", str(tmp), *objs, "-lcuda", "-ldl"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

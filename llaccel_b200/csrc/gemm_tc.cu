@@ -16,9 +16,10 @@
 // error word, stops issuing work, drains the copies it started and frees its TMEM.
 //
 // Split-K: with ksplit > 1, the CTAs of a thread-block cluster (cluster dims 1 x ksplit)
-// take disjoint K ranges; each writes its accumulator tile to its own shared memory and
-// the cluster's rank-0 CTA sums the partials over DSMEM before the epilogue (integer
-// addition: exact in any order).  No TMA multicast is used anywhere.
+// take disjoint K ranges; each writes its accumulator tile to its own shared memory, and
+// each CTA then owns a share of the tile's 16-channel chunks, summing the partials of every
+// CTA of the cluster over DSMEM before its epilogue (integer addition: exact in any order).
+// Every TMA load here is a plain single-CTA load.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -270,8 +271,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   // per-channel requant parameters
   for (int i = threadIdx.x; i < NT; i += blockDim.x) {
     const int n = n0 + i;
-    s_M[i] = n < a.N ? (uint32_t)a.rq[2 * n] : 0u;
-    s_S[i] = n < a.N ? a.rq[2 * n + 1] : 0;
+    s_M[i] = (n < a.N && a.rq) ? (uint32_t)a.rq[2 * n] : 0u;
+    s_S[i] = (n < a.N && a.rq) ? a.rq[2 * n + 1] : 0;
     s_bias[i] = (n < a.N && a.bias) ? (int64_t)a.bias[n] : 0;
   }
   if (a.epi == EPI_SILU || a.gated)
@@ -458,6 +459,19 @@ __global__ void __launch_bounds__(kThreads, 2)
           i8 = a.seg_i8[sgi];
           cnt = min(16, a.seg_start[sgi + 1] - nb);
         }
+        if (a.out_i32) {
+          // tensor-parallel partial sums: raw accumulators, 64 bytes per row chunk
+          int32_t* p = reinterpret_cast<int32_t*>(dst) + (int64_t)r * ld + col;
+          if (cnt == 16) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              reinterpret_cast<uint4*>(p)[k] = make_uint4((uint32_t)acc[4 * k], (uint32_t)acc[4 * k + 1],
+                                                          (uint32_t)acc[4 * k + 2], (uint32_t)acc[4 * k + 3]);
+          } else {
+            for (int j = 0; j < cnt; ++j) p[j] = acc[j];
+          }
+          continue;
+        }
         int32_t o[16];
         if (i8) {
 #pragma unroll
@@ -489,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int n = nb + j;
             if (j < cnt && n < a.amax_vocab) {
               const unsigned long long key =
-                  ((unsigned long long)(uint32_t)(o[j] + 32768) << 32) | (0xFFFFFFFFu - (uint32_t)n);
+                  ((unsigned long long)(uint32_t)(o[j] + 32768) << 32) | (0xFFFFFFFFu - (uint32_t)(n + a.amax_base));
               best = key > best ? key : best;
             }
           }

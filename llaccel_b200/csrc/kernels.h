@@ -56,8 +56,12 @@ cudaError_t launch_mul(const int16_t* a, const int16_t* b, int16_t* y, int64_t n
 cudaError_t launch_silu(const int16_t* x, int16_t* y, int64_t n, int64_t Mi, int Si, int sh_out,
                         const uint16_t* luts, cudaStream_t st);
 
-// logits [R][ld] i16 -> argmax over the first `vocab` entries (lowest index on ties)
-cudaError_t launch_argmax(const int16_t* logits, int R, int ld, int vocab, int32_t* out, cudaStream_t st);
+// logits [R][ld] i16 -> argmax over the first `vocab` entries (lowest index on ties).
+// With `keys` non-null the row's packed key (logit + 32768) << 32 | (0xFFFFFFFF - (base + n))
+// goes to keys[r] instead (a vocabulary shard starting at global channel `base`; the max of
+// the shards' keys is the global argmax), and `out` is not written.
+cudaError_t launch_argmax(const int16_t* logits, int R, int ld, int vocab, int base, int32_t* out,
+                          unsigned long long* keys, cudaStream_t st);
 
 // dst[i][:] = src[idx[i]][:] for i < n (row bytes multiple of 16)
 cudaError_t launch_gather_rows(const void* src, void* dst, const int32_t* idx, int n, int row_bytes,
@@ -72,9 +76,10 @@ struct LinearArgs {
   const int32_t* bias;  // [N] or null
   const int32_t* rq;    // [N][2] {M, S}
   const int16_t* aux;   // [R][N] i16 (RESADD / MUL) or null
-  void* out;            // [R][N] i16, or i8 when out_i8
+  void* out;            // [R][N] i16, or i8 when out_i8, or raw i32 sums when out_i32
   int R, N, K;
   int out_i8;
+  int out_i32;          // tensor-parallel partial: store sum_k A*W as int32, no bias / requant
   int epi;
   int64_t silu_Mi;
   int silu_Si, silu_sh;
@@ -101,9 +106,17 @@ struct LinearArgs {
   // Fused argmax (model output linear): per row, the max over channels n < amax_vocab of
   // key = (logit + 32768) << 32 | (0xFFFFFFFF - n) is folded into amax_key[r] with a 64-bit
   // atomicMax (largest logit, lowest index on ties).  amax_key must be zero beforehand.
+  // amax_base: global index of channel 0 (a vocabulary shard under tensor parallelism).
   unsigned long long* amax_key;
   int amax_vocab;
+  int amax_base;
 };
+
+// Tensor-parallel requant: acc [R][N] i32 (the all-reduced partial sums of a row-split
+// linear) -> bias, per-channel requant and epilogue exactly as the linear epilogue does,
+// into out [R][N] (i16, or i8 when a.out_i8).  Reads a.bias / a.rq / a.aux / a.epi /
+// silu / aux_shift / luts / out_i8 / narrow; a.A, a.W and a.K are unused.
+cudaError_t launch_requant(const int32_t* acc, const LinearArgs& a, cudaStream_t st);
 
 // CUDA-core paths: 0 = auto, 1 = GEMV (small R), 2 = tiled dp4a
 cudaError_t launch_linear(const LinearArgs& a, int path, cudaStream_t st);

@@ -20,6 +20,7 @@
 namespace llx {
 
 __device__ __forceinline__ int64_t linear_epilogue(int32_t acc, int r, int n, const LinearArgs& a) {
+  if (a.out_i32) return acc;  // tensor-parallel partial sums
   int64_t v = acc;
   if (a.bias) v += a.bias[n];
   const int64_t M = a.rq[2 * n];
@@ -35,7 +36,9 @@ __device__ __forceinline__ int64_t linear_epilogue(int32_t acc, int r, int n, co
 }
 
 __device__ __forceinline__ void store_out(const LinearArgs& a, int r, int n, int64_t v) {
-  if (a.out_i8)
+  if (a.out_i32)
+    reinterpret_cast<int32_t*>(a.out)[(int64_t)r * a.N + n] = (int32_t)v;
+  else if (a.out_i8)
     reinterpret_cast<int8_t*>(a.out)[(int64_t)r * a.N + n] = (int8_t)v;
   else
     reinterpret_cast<int16_t*>(a.out)[(int64_t)r * a.N + n] = (int16_t)v;

@@ -364,16 +364,17 @@ cudaError_t launch_silu(const int16_t* x, int16_t* y, int64_t n, int64_t Mi, int
 }
 
 // ---- argmax over the first `vocab` logits, lowest index on ties (NUMERICS.md:207-208) --------
-__global__ void k_argmax(const int16_t* __restrict__ logits, int ld, int vocab, int32_t* __restrict__ out) {
+__global__ void k_argmax(const int16_t* __restrict__ logits, int ld, int vocab, int base, int32_t* __restrict__ out,
+                         unsigned long long* __restrict__ keys) {
   pdl_trigger();
   pdl_wait();
   const int r = blockIdx.x;
   const int16_t* row = logits + (int64_t)r * ld;
-  // key: value in the high half, inverted index in the low half -> max key = first max
+  // key: value in the high half, inverted global index in the low half -> max key = first max
   unsigned long long best = 0;
   for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
     const unsigned long long key =
-        ((unsigned long long)(uint32_t)((int32_t)row[i] + 32768) << 32) | (0xFFFFFFFFu - (uint32_t)i);
+        ((unsigned long long)(uint32_t)((int32_t)row[i] + 32768) << 32) | (0xFFFFFFFFu - (uint32_t)(base + i));
     best = key > best ? key : best;
   }
 #pragma unroll
@@ -393,13 +394,78 @@ __global__ void k_argmax(const int16_t* __restrict__ logits, int ld, int vocab, 
       const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
       best = other > best ? other : best;
     }
-    if (lane == 0) out[r] = (int32_t)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
+    if (lane == 0) {
+      if (keys)
+        keys[r] = best;
+      else
+        out[r] = (int32_t)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
+    }
   }
 }
 
-cudaError_t launch_argmax(const int16_t* logits, int R, int ld, int vocab, int32_t* out, cudaStream_t st) {
+cudaError_t launch_argmax(const int16_t* logits, int R, int ld, int vocab, int base, int32_t* out,
+                          unsigned long long* keys, cudaStream_t st) {
   if (R <= 0) return cudaSuccess;
-  { const cudaError_t e_ = launch_k(k_argmax, dim3(R), dim3(512), 0, st, logits, ld, vocab, out); if (e_ != cudaSuccess) return e_; }
+  { const cudaError_t e_ = launch_k(k_argmax, dim3(R), dim3(512), 0, st, logits, ld, vocab, base, out, keys); if (e_ != cudaSuccess) return e_; }
+  return cudaGetLastError();
+}
+
+// ---- tensor-parallel requant of all-reduced partial sums -----------------------------------
+// Eight channels per thread: one 32-byte load of accumulators, one 16-byte (i16) or 8-byte
+// (i8) store.  N is a multiple of 8, so a group never straddles two rows.
+__global__ void k_requant(const int32_t* __restrict__ acc, LinearArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t groups = (int64_t)a.R * a.N / 8;
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < groups; g += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e0 = g * 8;
+    const int n0 = (int)(e0 % a.N);
+    const uint4 u0 = reinterpret_cast<const uint4*>(acc + e0)[0];
+    const uint4 u1 = reinterpret_cast<const uint4*>(acc + e0)[1];
+    const int32_t v[8] = {(int32_t)u0.x, (int32_t)u0.y, (int32_t)u0.z, (int32_t)u0.w,
+                          (int32_t)u1.x, (int32_t)u1.y, (int32_t)u1.z, (int32_t)u1.w};
+    int32_t o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int n = n0 + j;
+      int64_t t = (int64_t)v[j] + (a.bias ? (int64_t)a.bias[n] : 0);
+      t = mulshift(t, (int64_t)(uint32_t)a.rq[2 * n], a.rq[2 * n + 1]);
+      if (a.out_i8) {
+        o[j] = (int32_t)sat8(t);
+        continue;
+      }
+      t = sat16(t);
+      switch (a.epi) {
+        case EPI_RESADD: t = sat16(t + (int64_t)a.aux[e0 + j]); break;
+        case EPI_SILU: t = silu16(t, a.silu_Mi, a.silu_Si, a.silu_sh, a.luts + kLutSig); break;
+        case EPI_MUL: t = sat16(rshr(t * (int64_t)a.aux[e0 + j], a.aux_shift)); break;
+        default: break;
+      }
+      o[j] = (int32_t)t;
+    }
+    if (a.out_i8) {
+      uint2 w;
+      w.x = (uint32_t)(uint8_t)o[0] | (uint32_t)(uint8_t)o[1] << 8 | (uint32_t)(uint8_t)o[2] << 16 |
+            (uint32_t)(uint8_t)o[3] << 24;
+      w.y = (uint32_t)(uint8_t)o[4] | (uint32_t)(uint8_t)o[5] << 8 | (uint32_t)(uint8_t)o[6] << 16 |
+            (uint32_t)(uint8_t)o[7] << 24;
+      *reinterpret_cast<uint2*>(reinterpret_cast<int8_t*>(a.out) + e0) = w;
+    } else {
+      uint4 w;
+      w.x = (uint32_t)(uint16_t)o[0] | (uint32_t)(uint16_t)o[1] << 16;
+      w.y = (uint32_t)(uint16_t)o[2] | (uint32_t)(uint16_t)o[3] << 16;
+      w.z = (uint32_t)(uint16_t)o[4] | (uint32_t)(uint16_t)o[5] << 16;
+      w.w = (uint32_t)(uint16_t)o[6] | (uint32_t)(uint16_t)o[7] << 16;
+      *reinterpret_cast<uint4*>(reinterpret_cast<int16_t*>(a.out) + e0) = w;
+    }
+  }
+}
+
+cudaError_t launch_requant(const int32_t* acc, const LinearArgs& a, cudaStream_t st) {
+  const int64_t groups = (int64_t)a.R * a.N / 8;
+  if (groups <= 0) return cudaSuccess;
+  const int blocks = (int)std::min<int64_t>((groups + 255) / 256, 148 * 8);
+  { const cudaError_t e_ = launch_k(k_requant, dim3(blocks), dim3(256), 0, st, acc, a); if (e_ != cudaSuccess) return e_; }
   return cudaGetLastError();
 }
 

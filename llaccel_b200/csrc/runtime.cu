@@ -28,6 +28,7 @@
 #include <vector>
 
 #include "../../include/llx.h"
+#include "collective.h"
 #include "json.hpp"
 #include "kernels.h"
 #include "launch.cuh"
@@ -75,7 +76,12 @@ struct ActInfo {
   int elem = 2;
 };
 
-enum class SK { Embed, RmsNorm, Quant, Linear, Rope, KvWrite, Attention, Add, Mul, Silu, LinearGroup, Gated, RopeGroup };
+enum class SK {
+  Embed, RmsNorm, Quant, Linear, Rope, KvWrite, Attention, Add, Mul, Silu, LinearGroup, Gated, RopeGroup,
+  // tensor parallelism (graphs from llaccel_b200.tp.shard): int32 partial sums of a row-split
+  // linear, their in-place all-reduce, and the requant + epilogue of the reduced sums
+  LinearPartial, AllReduce, Requant
+};
 
 struct Step {
   SK kind;
@@ -161,6 +167,11 @@ struct llx_model {
   uint8_t* d_blob = nullptr;
   uint16_t* d_luts = nullptr;  // numerics.cuh kLut* layout
   int sms = 148;
+  // tensor parallelism: this rank's vocabulary shard is global channels
+  // [vocab_base, vocab_base + vocab_padded) of vocab_padded_full; tp = null on one GPU
+  int tp_rank = 0, tp_world = 1, vocab_base = 0, vocab_padded_full = 0;
+  llx::TpComm* tp = nullptr;
+  int n_sessions = 0;
 };
 
 namespace llx {
@@ -278,6 +289,11 @@ static void check_rq_table(const std::vector<uint8_t>& blob, const TensorSpec& t
     check_shift(p[2 * n + 1], ctx + " channel " + std::to_string(n));
   }
 }
+
+// rq table, bias, out_dtype and epilogue of a linear (or of the requant of a row-split
+// linear's reduced sums) over N channels; returns max |bias|
+static int64_t parse_rq_epilogue(llx_model* m, const json::Value& op, Step& s, const std::vector<uint8_t>& blob,
+                                 const std::string& ctx);
 
 static int64_t append_blob(std::vector<uint8_t>& blob, const void* src, size_t n) {
   const size_t off = (blob.size() + 63) & ~size_t(63);
@@ -421,6 +437,49 @@ static void fuse_steps(llx_model* m, std::vector<uint8_t>& blob) {
   st.swap(out);
 }
 
+static int64_t parse_rq_epilogue(llx_model* m, const json::Value& op, Step& s, const std::vector<uint8_t>& blob,
+                                 const std::string& ctx) {
+  const TensorSpec& rq = tensor(m, sval(op, "rq"), DT::RQ, ctx);
+  require(rq.count == s.N, LLX_ERR_INVALID, ctx + ": rq table size != N");
+  check_rq_table(blob, rq, ctx);
+  s.rq_off = rq.offset;
+  const std::string bias = sval_or(op, "bias", "");
+  int64_t max_bias = 0;
+  if (!bias.empty()) {
+    const TensorSpec& b = tensor(m, bias, DT::I32, ctx);
+    require(b.count == s.N, LLX_ERR_INVALID, ctx + ": bias size != N");
+    s.bias_off = b.offset;
+    const int32_t* bp = reinterpret_cast<const int32_t*>(blob.data() + b.offset);
+    for (int64_t n = 0; n < b.count; ++n) max_bias = std::max<int64_t>(max_bias, std::llabs((long long)bp[n]));
+  }
+  const std::string od = sval_or(op, "out_dtype", "i16");
+  const std::string ep = sval_or(op, "epilogue", "none");
+  require(od == "i16" || od == "i8", LLX_ERR_INVALID, ctx + ": unknown out_dtype " + od);
+  s.out_i8 = od == "i8";
+  if (s.out_i8) require(ep == "none", LLX_ERR_INVALID, "i8 output is only valid with epilogue none");
+  if (ep == "none") {
+    s.epi = EPI_NONE;
+  } else if (ep == "resadd" || ep == "mul") {
+    s.epi = ep == "resadd" ? EPI_RESADD : EPI_MUL;
+    s.in2 = act_lookup(m, sval(op, "aux"), ctx);
+    require(m->acts[s.in2].elem == 2 && m->acts[s.in2].cols == s.N, LLX_ERR_INVALID, ctx + ": aux must be i16 [M][N]");
+    s.aux_shift = (int)ival_or(op, "aux_shift", 0);
+    check_shift(s.aux_shift, ctx);
+  } else if (ep == "silu") {
+    s.epi = EPI_SILU;
+    const json::Value& sp = op.at("silu");
+    s.silu_Mi = ival(sp, "Mi");
+    s.silu_Si = (int)ival(sp, "Si");
+    s.silu_sh = (int)ival(sp, "sh_out");
+    check_mult(s.silu_Mi, ctx);
+    check_shift(s.silu_Si, ctx);
+    check_shift(s.silu_sh, ctx);
+  } else {
+    throw Error(LLX_ERR_INVALID, "unknown epilogue '" + ep + "'");
+  }
+  return max_bias;
+}
+
 static void build_plan(llx_model* m, const json::Value& g, std::vector<uint8_t>& blob) {
   const json::Value& ops = g.at("ops");
   require(ops.kind == json::Value::Array, LLX_ERR_INVALID, "qgraph 'ops' is not a list");
@@ -505,58 +564,41 @@ static void build_plan(llx_model* m, const json::Value& g, std::vector<uint8_t>&
       s.out = out;
       s.Mq = M;
       s.Sq = (int)S;
-    } else if (k == "linear") {
-      s.kind = SK::Linear;
+    } else if (k == "linear" || k == "linear_partial") {
+      s.kind = k == "linear" ? SK::Linear : SK::LinearPartial;
       s.in = act_lookup(m, sval(op, "in"), ctx);
       require(m->acts[s.in].elem == 1, LLX_ERR_INVALID, ctx + ": linear input must be i8");
       const TensorSpec& w = tensor(m, sval(op, "w"), DT::I8, ctx);
       s.N = (int)ival(op, "N");
       s.K = (int)ival(op, "K");
       require(w.shape.size() == 2 && w.shape[0] == s.N && w.shape[1] == s.K && m->acts[s.in].cols == s.K,
-              LLX_ERR_INVALID, "linear " + sval(op, "out") + ": shapes do not match N/K");
+              LLX_ERR_INVALID, k + " " + sval(op, "out") + ": shapes do not match N/K");
       require(s.K % 16 == 0 && s.N % 8 == 0, LLX_ERR_UNSUPPORTED, ctx + ": N must be a multiple of 8, K of 16");
-      const TensorSpec& rq = tensor(m, sval(op, "rq"), DT::RQ, ctx);
-      require(rq.count == s.N, LLX_ERR_INVALID, ctx + ": rq table size != N");
-      check_rq_table(blob, rq, ctx);
       s.w_off = w.offset;
-      s.rq_off = rq.offset;
-      const std::string bias = sval_or(op, "bias", "");
-      int64_t max_bias = 0;
-      if (!bias.empty()) {
-        const TensorSpec& b = tensor(m, bias, DT::I32, ctx);
-        require(b.count == s.N, LLX_ERR_INVALID, ctx + ": bias size != N");
-        s.bias_off = b.offset;
-        const int32_t* bp = reinterpret_cast<const int32_t*>(blob.data() + b.offset);
-        for (int64_t n = 0; n < b.count; ++n) max_bias = std::max<int64_t>(max_bias, std::llabs((long long)bp[n]));
-      }
-      // |sum_k a*w| <= K * 128 * 128; the bias add stays in 32 bits when the total cannot wrap
-      s.narrow = (int64_t)s.K * 16384 + max_bias < (1ll << 31) ? 1 : 0;
-      const std::string od = sval_or(op, "out_dtype", "i16");
-      const std::string ep = sval_or(op, "epilogue", "none");
-      require(od == "i16" || od == "i8", LLX_ERR_INVALID, ctx + ": unknown out_dtype " + od);
-      s.out_i8 = od == "i8";
-      if (s.out_i8) require(ep == "none", LLX_ERR_INVALID, "i8 output is only valid with epilogue none");
-      if (ep == "none") {
-        s.epi = EPI_NONE;
-      } else if (ep == "resadd" || ep == "mul") {
-        s.epi = ep == "resadd" ? EPI_RESADD : EPI_MUL;
-        s.in2 = act_lookup(m, sval(op, "aux"), ctx);
-        require(m->acts[s.in2].elem == 2 && m->acts[s.in2].cols == s.N, LLX_ERR_INVALID,
-                ctx + ": aux must be i16 [M][N]");
-        s.aux_shift = (int)ival_or(op, "aux_shift", 0);
-        check_shift(s.aux_shift, ctx);
-      } else if (ep == "silu") {
-        s.epi = EPI_SILU;
-        const json::Value& sp = op.at("silu");
-        s.silu_Mi = ival(sp, "Mi");
-        s.silu_Si = (int)ival(sp, "Si");
-        s.silu_sh = (int)ival(sp, "sh_out");
-        check_mult(s.silu_Mi, ctx);
-        check_shift(s.silu_Si, ctx);
-        check_shift(s.silu_sh, ctx);
+      if (s.kind == SK::LinearPartial) {
+        s.out = act_define(m, sval(op, "out"), s.N, 4);
       } else {
-        throw Error(LLX_ERR_INVALID, "unknown epilogue '" + ep + "'");
+        const int64_t max_bias = parse_rq_epilogue(m, op, s, blob, ctx);
+        // |sum_k a*w| <= K * 128 * 128; the bias add stays in 32 bits when the total cannot wrap
+        s.narrow = (int64_t)s.K * 16384 + max_bias < (1ll << 31) ? 1 : 0;
+        s.out = act_define(m, sval(op, "out"), s.N, s.out_i8 ? 1 : 2);
       }
+    } else if (k == "allreduce") {
+      s.kind = SK::AllReduce;
+      s.in = act_lookup(m, sval(op, "in"), ctx);
+      require(m->acts[s.in].elem == 4, LLX_ERR_INVALID, ctx + ": all-reduce input must be int32 partial sums");
+      require(sval(op, "out") == sval(op, "in"), LLX_ERR_UNSUPPORTED, ctx + ": the all-reduce is in place (out == in)");
+      require(sval_or(op, "reduce", "sum") == "sum", LLX_ERR_UNSUPPORTED, ctx + ": only sum all-reduces exist");
+      s.N = m->acts[s.in].cols;
+      s.out = s.in;
+    } else if (k == "requant") {
+      s.kind = SK::Requant;
+      s.in = act_lookup(m, sval(op, "in"), ctx);
+      s.N = (int)ival(op, "N");
+      require(m->acts[s.in].elem == 4 && m->acts[s.in].cols == s.N, LLX_ERR_INVALID,
+              ctx + ": requant input must be int32 [M][N]");
+      require(s.N % 8 == 0, LLX_ERR_UNSUPPORTED, ctx + ": N must be a multiple of 8");
+      parse_rq_epilogue(m, op, s, blob, ctx);
       s.out = act_define(m, sval(op, "out"), s.N, s.out_i8 ? 1 : 2);
     } else if (k == "rope") {
       s.kind = SK::Rope;
@@ -701,7 +743,18 @@ static void load_model(llx_model* m, const std::string& dir) {
   require(m->prefill_m >= 1 && m->prefill_m <= 16 && m->max_seq % m->prefill_m == 0, LLX_ERR_INVALID,
           "max_seq must be divisible by prefill_m in [1,16]");
   require(m->dim > 0 && m->dim % 16 == 0, LLX_ERR_UNSUPPORTED, "dim must be a positive multiple of 16");
-  require(m->vocab > 0 && m->vocab <= m->vocab_padded, LLX_ERR_INVALID, "vocab exceeds vocab_padded");
+  m->vocab_padded_full = m->vocab_padded;
+  if (const json::Value* tp = md.find("tp")) {
+    // a rank graph of a tensor-parallel group: the output is this rank's vocabulary shard
+    m->tp_rank = (int)ival(*tp, "rank");
+    m->tp_world = (int)ival(*tp, "world");
+    m->vocab_base = (int)ival(*tp, "vocab_offset");
+    m->vocab_padded_full = (int)ival(*tp, "vocab_padded_full");
+    require(m->tp_world >= 1 && m->tp_rank >= 0 && m->tp_rank < m->tp_world, LLX_ERR_INVALID, "model.tp: bad rank/world");
+    require(m->vocab_base >= 0 && m->vocab_base + m->vocab_padded <= m->vocab_padded_full, LLX_ERR_INVALID,
+            "model.tp: vocabulary shard outside vocab_padded_full");
+  }
+  require(m->vocab > 0 && m->vocab <= m->vocab_padded_full, LLX_ERR_INVALID, "vocab exceeds vocab_padded");
   const std::string wfile = g.find("weights_file") ? g.at("weights_file").as_str() : "qweights.bin";
   std::vector<uint8_t> blob;
   {
@@ -793,6 +846,8 @@ struct llx_session {
   std::map<std::tuple<const void*, int64_t, int64_t, int>, CUtensorMap> tmaps;
   int32_t* d_fault = nullptr;  // nonzero: a tensor-core pipeline wait timed out
   unsigned long long* d_amax_key = nullptr;  // [B*max_rows] fused argmax keys of the output linear
+  int16_t* d_gather = nullptr;  // tensor parallelism: all-gathered logits shards [world][rows][vocab_padded]
+  size_t gather_n = 0;
   cudaGraphExec_t decode_exec = nullptr;
   int decode_launches = 0;
   int last_R = 0, last_Rtail = 0;
@@ -883,10 +938,37 @@ static bool output_argmax_fused(const llx_model* m, int R) {
   return false;
 }
 
-static cudaError_t launch_output_argmax(llx_session* s, const void* logits, int R) {
+// channels of this rank's output that are real vocabulary entries (all of them on one GPU)
+static int local_vocab(const llx_model* m) {
+  return std::max(0, std::min(m->vocab_padded, m->vocab - m->vocab_base));
+}
+
+static void tp_check(bool ok, const std::string& err) {
+  if (!ok) throw Error(LLX_ERR_CUDA, err);
+}
+
+// argmax tokens of R output rows into d_argmax.  Under tensor parallelism every rank holds
+// packed keys of its vocabulary shard (global indices); a uint64 max all-reduce picks the
+// global first maximum before the keys are decoded.
+static void launch_output_argmax(llx_session* s, const void* logits, int R) {
   const llx_model* m = s->m;
-  if (output_argmax_fused(m, R)) return launch_amax_finish(s->d_amax_key, s->d_argmax, R, s->st);
-  return launch_argmax((const int16_t*)logits, R, m->vocab_padded, m->vocab, s->d_argmax, s->st);
+  const bool fused = output_argmax_fused(m, R);
+  cudaError_t e = cudaSuccess;
+  if (m->tp) {
+    if (!fused)
+      e = launch_argmax((const int16_t*)logits, R, m->vocab_padded, local_vocab(m), m->vocab_base, nullptr,
+                        s->d_amax_key, s->st);
+    if (e == cudaSuccess) {
+      std::string err;
+      tp_check(tp_allreduce_max_u64(m->tp, s->d_amax_key, R, s->st, &err), err);
+      e = launch_amax_finish(s->d_amax_key, s->d_argmax, R, s->st);
+    }
+  } else if (fused) {
+    e = launch_amax_finish(s->d_amax_key, s->d_argmax, R, s->st);
+  } else {
+    e = launch_argmax((const int16_t*)logits, R, m->vocab_padded, m->vocab, 0, s->d_argmax, nullptr, s->st);
+  }
+  if (e != cudaSuccess) throw Error(LLX_ERR_CUDA, std::string("argmax launch failed: ") + cudaGetErrorString(e));
 }
 
 static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, int M) {
@@ -929,7 +1011,8 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
         const int path = gemm_path_for(m, R);
         if (path == 3 && x.out == m->output_act) {
           a.amax_key = s->d_amax_key;
-          a.amax_vocab = m->vocab;
+          a.amax_vocab = local_vocab(m);
+          a.amax_base = m->vocab_base;
         }
         if (path == 3) {
           int nt = 16, ks = 1;
@@ -940,6 +1023,52 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
         } else {
           e = launch_linear(a, path, st);
         }
+        break;
+      }
+      case SK::LinearPartial: {
+        LinearArgs a{};
+        a.A = (const int8_t*)P(x.in);
+        a.W = (const int8_t*)dptr(m, x.w_off);
+        a.out = P(x.out);
+        a.R = R;
+        a.N = x.N;
+        a.K = x.K;
+        a.out_i32 = 1;
+        a.luts = m->d_luts;
+        const int path = gemm_path_for(m, R);
+        if (path == 3) {
+          int nt = 16, ks = 1;
+          pick_tc_tiling(R, x.N, x.K, m->sms, &nt, &ks);
+          const CUtensorMap& ma = tmap(s, a.A, (int64_t)bd.rows[x.in], x.K, 128);
+          const CUtensorMap& mw = tmap(s, a.W, x.N, x.K, nt);
+          e = launch_linear_tc(ma, mw, a, nt, ks, s->d_fault, st);
+        } else {
+          e = launch_linear(a, path, st);
+        }
+        break;
+      }
+      case SK::AllReduce: {
+        if (!m->tp) return 0;  // a one-rank group: the partial sums are already complete
+        std::string err;
+        tp_check(tp_allreduce_sum_i32(m->tp, (int32_t*)P(x.in), (size_t)R * x.N, st, &err), err);
+        return 1;
+      }
+      case SK::Requant: {
+        LinearArgs a{};
+        a.bias = (const int32_t*)dptr(m, x.bias_off);
+        a.rq = (const int32_t*)dptr(m, x.rq_off);
+        a.aux = (const int16_t*)P(x.in2);
+        a.out = P(x.out);
+        a.R = R;
+        a.N = x.N;
+        a.out_i8 = x.out_i8;
+        a.epi = x.epi;
+        a.silu_Mi = x.silu_Mi;
+        a.silu_Si = x.silu_Si;
+        a.silu_sh = x.silu_sh;
+        a.aux_shift = x.aux_shift;
+        a.luts = m->d_luts;
+        e = launch_requant((const int32_t*)P(x.in), a, st);
         break;
       }
       case SK::Rope: {
@@ -1241,26 +1370,53 @@ static void run_launch(llx_session* s, int M, int pos, bool with_embed, const in
     }
     enqueue_steps(s, bt, m->tail_start, m->steps.size(), Rtail, n_rec);
   }
-  const cudaError_t e = launch_output_argmax(s, bd.p[m->output_act], Rtail);
-  if (e != cudaSuccess) throw Error(LLX_ERR_CUDA, cudaGetErrorString(e));
+  launch_output_argmax(s, bd.p[m->output_act], Rtail);
   s->last_R = R;
   s->last_Rtail = Rtail;
   s->last_tail = tail;
 }
 
-static void copy_outputs(llx_session* s, int rows, int16_t* logits, int32_t* argmax) {
+// logits of the last launch's first `rows` output rows -> host [rows][vocab_padded_full].
+// Under tensor parallelism the ranks' vocabulary shards are all-gathered first (a
+// collective: every rank of the group makes the same call).
+static void fetch_logits(llx_session* s, int rows, int16_t* host) {
   llx_model* m = s->m;
   const Binding bd = bind(s, false);
-  if (logits) ensure_i16(s, (size_t)rows * m->vocab_padded);
+  const size_t vl = m->vocab_padded;
+  if (!m->tp) {
+    ensure_i16(s, (size_t)rows * vl);
+    LLX_CUDA(cudaMemcpyAsync(s->h_i16, bd.p[m->output_act], sizeof(int16_t) * rows * vl, cudaMemcpyDeviceToHost,
+                             s->st));
+    LLX_CUDA(cudaStreamSynchronize(s->st));
+    std::memcpy(host, s->h_i16, sizeof(int16_t) * rows * vl);
+    return;
+  }
+  const size_t W = m->tp_world, n = W * rows * vl;
+  if (s->gather_n < n) {
+    LLX_CUDA(cudaStreamSynchronize(s->st));
+    if (s->d_gather) cudaFree(s->d_gather);
+    s->d_gather = nullptr;
+    s->gather_n = 0;
+    LLX_CUDA(cudaMalloc(&s->d_gather, n * sizeof(int16_t)));
+    s->gather_n = n;
+  }
+  ensure_i16(s, n);
+  std::string err;
+  tp_check(tp_allgather_bytes(m->tp, bd.p[m->output_act], s->d_gather, sizeof(int16_t) * rows * vl, s->st, &err), err);
+  LLX_CUDA(cudaMemcpyAsync(s->h_i16, s->d_gather, sizeof(int16_t) * n, cudaMemcpyDeviceToHost, s->st));
+  LLX_CUDA(cudaStreamSynchronize(s->st));
+  const size_t full = m->vocab_padded_full;
+  for (size_t r = 0; r < (size_t)rows; ++r)
+    for (size_t w = 0; w < W; ++w)
+      std::memcpy(host + r * full + w * vl, s->h_i16 + (w * rows + r) * vl, sizeof(int16_t) * vl);
+}
+
+static void copy_outputs(llx_session* s, int rows, int16_t* logits, int32_t* argmax) {
   if (argmax)
     LLX_CUDA(cudaMemcpyAsync(s->h_am, s->d_argmax, sizeof(int32_t) * rows, cudaMemcpyDeviceToHost, s->st));
-  if (logits) {
-    LLX_CUDA(cudaMemcpyAsync(s->h_i16, bd.p[m->output_act], sizeof(int16_t) * rows * m->vocab_padded,
-                             cudaMemcpyDeviceToHost, s->st));
-  }
   LLX_CUDA(cudaStreamSynchronize(s->st));
   if (argmax) std::memcpy(argmax, s->h_am, sizeof(int32_t) * rows);
-  if (logits) std::memcpy(logits, s->h_i16, sizeof(int16_t) * rows * m->vocab_padded);
+  if (logits) fetch_logits(s, rows, logits);
 }
 
 static void stage_tokens(llx_session* s, const int32_t* tokens, int n) {
@@ -1281,8 +1437,7 @@ static void build_decode_graph(llx_session* s) {
   int n = 0;
   try {
     n = enqueue_steps(s, bd, 0, m->steps.size(), s->B, 1);
-    cudaError_t e = launch_output_argmax(s, bd.p[m->output_act], s->B);
-    if (e != cudaSuccess) throw Error(LLX_ERR_CUDA, cudaGetErrorString(e));
+    launch_output_argmax(s, bd.p[m->output_act], s->B);
     LLX_CUDA(launch_k(k_decode_finalize, dim3(1), dim3(256), 0, s->st, (const int32_t*)s->d_argmax, s->d_tokens,
                       s->d_hist, s->d_pos, s->d_step, s->B, s->hist_cap));
   } catch (...) {
@@ -1298,8 +1453,14 @@ static void build_decode_graph(llx_session* s) {
 
 static void session_create(llx_model* m, int batch, int max_rows, int keep, llx_session* s) {
   require(batch >= 1, LLX_ERR_INVALID, "batch must be >= 1");
+  if (m->tp_world > 1) {
+    require(m->tp != nullptr, LLX_ERR_INVALID, "tensor-parallel rank graph: call llx_tp_init before creating a session");
+    // collectives of two sessions on one communicator could interleave differently per rank
+    require(m->n_sessions == 0, LLX_ERR_UNSUPPORTED, "a tensor-parallel model serves one session at a time");
+  }
   require(max_rows >= 1 && max_rows <= m->max_seq, LLX_ERR_INVALID, "max_rows must be in [1, max_seq]");
   s->m = m;
+  m->n_sessions++;
   s->B = batch;
   s->max_rows = max_rows;
   s->keep = keep != 0;
@@ -1344,11 +1505,14 @@ static void session_create(llx_model* m, int batch, int max_rows, int keep, llx_
 
 static void session_free(llx_session* s) {
   if (!s) return;
-  if (s->m) cudaSetDevice(s->m->device);
+  if (s->m) {
+    cudaSetDevice(s->m->device);
+    s->m->n_sessions--;
+  }
   if (s->st) cudaStreamSynchronize(s->st);
   if (s->decode_exec) cudaGraphExecDestroy(s->decode_exec);
   for (void* p : {(void*)s->arena, (void*)s->kv, (void*)s->d_tokens, (void*)s->d_rec, (void*)s->d_argmax,
-                  (void*)s->d_hist, (void*)s->d_pos, (void*)s->d_amax_key})
+                  (void*)s->d_hist, (void*)s->d_pos, (void*)s->d_amax_key, (void*)s->d_gather})
     if (p) cudaFree(p);
   for (void* p : {(void*)s->h_tok, (void*)s->h_rec, (void*)s->h_am, (void*)s->h_pos, (void*)s->h_i16})
     if (p) cudaFreeHost(p);
@@ -1416,6 +1580,7 @@ llx_status llx_model_load(const char* dir, const llx_opts* opts, llx_model** out
 
 void llx_model_destroy(llx_model* m) {
   if (!m) return;
+  tp_comm_destroy(m->tp);
   cudaSetDevice(m->device);
   if (m->d_blob) cudaFree(m->d_blob);
   if (m->d_luts) cudaFree(m->d_luts);
@@ -1432,7 +1597,6 @@ llx_status llx_model_get_info(const llx_model* m, llx_model_info* o) {
     o->head_dim = m->head_dim;
     o->ffn = m->ffn;
     o->vocab = m->vocab;
-    o->vocab_padded = m->vocab_padded;
     o->max_seq = m->max_seq;
     o->prefill_m = m->prefill_m;
     o->E_RES = m->E_RES;
@@ -1441,6 +1605,35 @@ llx_status llx_model_get_info(const llx_model* m, llx_model_info* o) {
     o->n_steps = (int)m->steps.size();
     o->n_activations = (int)m->acts.size();
     o->weight_bytes = m->blob_bytes;
+    o->vocab_padded = m->vocab_padded_full;
+    o->tp_world = m->tp_world;
+    o->tp_rank = m->tp_rank;
+    o->vocab_base = m->vocab_base;
+    o->vocab_local = m->vocab_padded;
+  });
+}
+
+llx_status llx_tp_unique_id(void* id) {
+  return guarded([&] {
+    require(id, LLX_ERR_INVALID, "null argument");
+    std::string err;
+    require(tp_unique_id(id, &err), LLX_ERR_CUDA, err);
+  });
+}
+
+llx_status llx_tp_init(llx_model* m, const void* id, int rank, int world) {
+  return guarded([&] {
+    require(m && id, LLX_ERR_INVALID, "null argument");
+    require(m->tp == nullptr, LLX_ERR_INVALID, "llx_tp_init: the model already has a communicator");
+    require(m->n_sessions == 0, LLX_ERR_INVALID, "llx_tp_init: call it before creating sessions");
+    require(world == m->tp_world && rank == m->tp_rank, LLX_ERR_INVALID,
+            "llx_tp_init: rank " + std::to_string(rank) + " of " + std::to_string(world) +
+                " does not match the graph's model.tp (rank " + std::to_string(m->tp_rank) + " of " +
+                std::to_string(m->tp_world) + ")");
+    std::string err;
+    TpComm* c = tp_comm_create(id, rank, world, m->device, &err);
+    require(c != nullptr, LLX_ERR_CUDA, err);
+    m->tp = c;
   });
 }
 
@@ -1547,7 +1740,7 @@ llx_status llx_generate(llx_session* s, const int32_t* prompts, int L, int n_tok
     const int n_dec = std::min(n_tokens, std::max(0, m->max_seq - L - 1));
     const int n_launch = n_chunks + n_dec;
     *n_launch_out = n_launch;
-    const int V = m->vocab, VP = m->vocab_padded;
+    const int V = m->vocab, VP = m->vocab_padded_full;
     std::vector<int32_t> tok, rec, am;
     std::vector<int16_t> lg;
     // ---- prefill: golden chunks c = 0..n_chunks-1, grouped into launches ----
@@ -1587,13 +1780,10 @@ llx_status llx_generate(llx_session* s, const int32_t* prompts, int L, int n_tok
       stage_tokens(s, nxt.data(), B);
       set_pos(s, L);
       if (logits) lg.resize((size_t)B * VP);
-      const Binding bd = bind(s, false);
       for (int i = 0; i < n_dec; ++i) {
         LLX_CUDA(cudaGraphLaunch(s->decode_exec, s->st));
         if (logits) {
-          LLX_CUDA(cudaMemcpyAsync(lg.data(), bd.p[m->output_act], sizeof(int16_t) * B * VP, cudaMemcpyDeviceToHost,
-                                   s->st));
-          LLX_CUDA(cudaStreamSynchronize(s->st));
+          fetch_logits(s, B, lg.data());
           for (int b = 0; b < B; ++b)
             std::memcpy(logits + ((size_t)b * n_launch + n_chunks + i) * V, lg.data() + (size_t)b * VP,
                         sizeof(int16_t) * V);
@@ -1707,6 +1897,15 @@ llx_status llx_profile_decode(llx_session* s, int pos, int iters, float* ms, dou
             b = R * x.H * x.D * (x.out2 >= 0 ? 5.0 : 4.0) + R * 2.0 * x.D + (x.write_k ? 1.0 * R * x.H * x.D : 0.0);
             break;
           case SK::KvWrite: b = (x.in >= 0 ? 2.0 : 1.0) * 2.0 * R * x.Hkv * x.D; break;
+          case SK::LinearPartial:
+            b = (double)x.N * x.K + (double)R * x.K + 4.0 * R * x.N;
+            o = 2.0 * R * x.N * x.K;
+            break;
+          case SK::AllReduce: b = 8.0 * R * x.N; break;  // read + write of the local buffer
+          case SK::Requant:
+            b = 4.0 * R * x.N + 8.0 * x.N + (x.bias_off >= 0 ? 4.0 * x.N : 0.0) + (double)R * x.N * (x.out_i8 ? 1 : 2) +
+                (x.in2 >= 0 ? 2.0 * R * x.N : 0.0);
+            break;
           case SK::Attention:
             b = 2.0 * R * x.Hkv * T * x.D + 2.0 * R * x.H * x.D;
             o = 4.0 * R * x.H * x.D * T;
@@ -1746,8 +1945,7 @@ llx_status llx_profile_decode(llx_session* s, int pos, int iters, float* ms, dou
         if (i < (int)m->steps.size()) {
           enqueue_steps(s, bd, i, i + 1, R, 1);
         } else {
-          const cudaError_t e = launch_output_argmax(s, bd.p[m->output_act], R);
-          if (e != cudaSuccess) throw Error(LLX_ERR_CUDA, cudaGetErrorString(e));
+          launch_output_argmax(s, bd.p[m->output_act], R);
         }
       }
       LLX_CUDA(cudaEventRecord(e1, s->st));

@@ -58,6 +58,8 @@ SIGNATURES = {
                                             C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
     "llx_last_error": (C.c_char_p, []),
     "llx_version": (C.c_char_p, []),
+    "llx_tp_unique_id": (C.c_int, [C.c_void_p]),
+    "llx_tp_init": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int]),
 }
 
 
@@ -68,7 +70,8 @@ class LlxOpts(C.Structure):
 class LlxModelInfo(C.Structure):
     _fields_ = [(n, C.c_int) for n in ("dim", "n_layers", "n_heads", "n_kv_heads", "head_dim", "ffn", "vocab",
                                         "vocab_padded", "max_seq", "prefill_m", "E_RES", "E_LOGIT", "n_ops",
-                                        "n_steps", "n_activations")] + [("weight_bytes", C.c_size_t)]
+                                        "n_steps", "n_activations")] + [("weight_bytes", C.c_size_t)] + \
+        [(n, C.c_int) for n in ("tp_world", "tp_rank", "vocab_base", "vocab_local")]
 
 
 class LlxError(RuntimeError):
@@ -107,6 +110,14 @@ def _check(lib, code: int) -> None:
     raise LlxError(code, msg)
 
 
+def tp_unique_id() -> bytes:
+    """A fresh NCCL unique id (128 bytes) for llx_tp_init; made on rank 0 and shared."""
+    lib = load_library()
+    buf = C.create_string_buffer(128)
+    _check(lib, lib.llx_tp_unique_id(buf))
+    return buf.raw
+
+
 def _p32(a: np.ndarray):
     return a.ctypes.data_as(_I32P)
 
@@ -122,9 +133,12 @@ class CudaModel:
 
     def __init__(self, qgraph_dir, *, batch: int = 1, device: int = 0, max_rows: int | None = None,
                  keep_acts: bool = False, fuse: bool = True, gemm_path: int = 0, pdl: bool = True,
-                 share: "CudaModel | None" = None) -> None:
+                 share: "CudaModel | None" = None, tp: "tuple[int, int, bytes] | None" = None) -> None:
         """`share`: reuse the weights already loaded by another CudaModel (same device); this
-        instance then owns only its session (KV cache, activations, stream)."""
+        instance then owns only its session (KV cache, activations, stream).
+        `tp`: (rank, world, unique_id) for a rank graph of a tensor-parallel group
+        (llaccel_b200.tp.shard); every rank of the group constructs its model together and
+        then makes the same calls in the same order."""
         self.lib = load_library()
         self.dir = Path(qgraph_dir)
         self.batch = int(batch)
@@ -136,6 +150,17 @@ class CudaModel:
             opts = LlxOpts(int(device), 1 if fuse else 0, int(gemm_path), 1 if pdl else 0)
             self._model = C.c_void_p()
             _check(self.lib, self.lib.llx_model_load(str(self.dir).encode(), C.byref(opts), C.byref(self._model)))
+            if tp is not None:
+                rank, world, uid = tp
+                uid_buf = C.create_string_buffer(bytes(uid), 128)
+                code = self.lib.llx_tp_init(self._model, uid_buf, int(rank), int(world))
+                if code != LLX_OK:
+                    msg = self.lib.llx_last_error().decode()
+                    self.lib.llx_model_destroy(self._model)
+                    self._model = None
+                    if code in (LLX_ERR_INVALID, LLX_ERR_RANGE):
+                        raise ValueError(msg)
+                    raise LlxError(code, msg)
         info = LlxModelInfo()
         _check(self.lib, self.lib.llx_model_get_info(self._model, C.byref(info)))
         self.info = info

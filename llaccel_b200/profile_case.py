@@ -1,11 +1,14 @@
 """A small decode case for profilers: one of the bench configs with a short prompt, so a
 capture holds a few GB on the device at most and ends by itself.
 
-    python -m llaccel_b200.profile_case --config c3 --batch 128 --prompt 32 --decode 3
+    python -m llaccel_b200.profile_case --config c3 --batch 128 --prompt 512 --max-rows 64 --decode 3
 
 Generates (or reuses) the config's artefact under --artefacts, prefills `batch` random
-prompts of `prompt` tokens, then runs `decode` device-resident decode launches and prints
-the first sequence's tokens.
+prompts of `prompt` tokens in launches of `max-rows` rows per sequence (default: the whole
+prompt in one launch), then runs `decode` device-resident decode launches and prints the
+first sequence's tokens.  With --max-rows 64 the bench's decode shapes (128 sequences at
+context ~512) hold about 1.3 GB on the device, so a capture stays small.  Tensor-core GEMM
+launches before the first decode launch: (prefill launches) x (4 per layer + 1).
 """
 from __future__ import annotations
 
@@ -23,15 +26,17 @@ def main(argv=None) -> None:
     ap.add_argument("--batch", type=int, default=128)
     ap.add_argument("--prompt", type=int, default=32)
     ap.add_argument("--decode", type=int, default=3)
+    ap.add_argument("--max-rows", type=int, default=0)
     ap.add_argument("--artefacts", default=os.environ.get("LLX_ARTEFACTS", str(Path(tempfile.gettempdir()) / "llx_artefacts")))
     a = ap.parse_args(argv)
     from llaccel_b200 import artefacts as A, build
     build.build()
     from llaccel_b200.cuda_backend import CudaModel
     d = A.ensure_artefact(a.config, a.artefacts, seed=0, fusion=True, device="cuda")
-    m = CudaModel(d, batch=a.batch, max_rows=a.prompt)
+    rows = a.max_rows or a.prompt
+    m = CudaModel(d, batch=a.batch, max_rows=rows)
     prompts = np.random.default_rng(0).integers(0, A.CONFIGS[a.config].vocab, (a.batch, a.prompt)).tolist()
-    recs = m.generate_batch(prompts, 0, with_logits=False)
+    recs = m.generate_batch(prompts, 0, with_logits=False, prefill_rows=rows)
     m.set_tokens([r["argmax_per_step"][-1] for r in recs])
     m.decode_async(a.prompt, a.decode)
     m.sync()

@@ -299,11 +299,16 @@ class OracleModel:
         """GEMM + bias + per-channel requant + epilogue (golden.py:316-342, NUMERICS.md:62-86)."""
         a = act[op["in"]]
         w = self.q.tensors[op["w"]]
-        rq = self.q.tensors[op["rq"]]
         N, K = int(op["N"]), int(op["K"])
         if w.shape != (N, K) or a.shape[1] != K:
             raise ValueError(f"linear {op['out']}: shapes A{a.shape} W{w.shape} vs N={N} K={K}")
-        acc = exact_matmul(a, w)
+        return self._requant(op, exact_matmul(a, w), act)
+
+    def _requant(self, op, acc, act):
+        """Bias (64-bit add), per-channel requant and epilogue of an int32 accumulator
+        (golden.py:325-342).  Shared by `linear` and by the tensor-parallel `requant` op,
+        which applies it to the all-reduced partial accumulators."""
+        rq = self.q.tensors[op["rq"]]
         if op.get("bias"):
             acc = acc + self.q.tensors[op["bias"]].astype(I64)[None, :]
         Mn = rq[:, 0].astype(I64)[None, :]
@@ -333,45 +338,64 @@ class OracleModel:
         if pos < 0 or pos + M > self.max_seq:
             raise ValueError(f"positions {pos}..{pos + M - 1} exceed max_seq={self.max_seq}")
         act = {self.q.input_name: rows}
-        T = self.q.tensors
         for op in self.q.ops:
-            kind = op["op"]
-            if kind == "rmsnorm":
-                x = act[op["in"]]
-                g = T[op["gamma"]]
-                heads = int(op.get("heads", 1))
-                if heads < 1 or x.shape[1] != heads * len(g):
-                    raise ValueError("RMSNorm head geometry mismatch")
-                y = rmsnorm(x.reshape(-1, len(g)), g, op["eps_t"], op["C"], op["sh_post"])
-                act[op["out"]] = y.reshape(x.shape)
-            elif kind == "quant":
-                act[op["out"]] = vquant(act[op["in"]], op["M"], op["S"])
-            elif kind == "linear":
-                act[op["out"]] = self._linear(op, act)
-            elif kind == "rope":
-                act[op["out"]] = rope(act[op["in"]], int(op["H"]), int(op["D"]), self.rope_cos, self.rope_sin, pos)
-            elif kind == "kv_write":
-                kc, vc = self.kv[int(op["layer"])]
-                Hkv, D = int(op["Hkv"]), int(op["D"])
-                k = act[op["k"]].reshape(M, Hkv, D)
-                v = act[op["v"]].reshape(M, Hkv, D)
-                kc[:, pos : pos + M] = k.transpose(1, 0, 2)
-                vc[:, pos : pos + M] = v.transpose(1, 0, 2)
-            elif kind == "attention":
-                kc, vc = self.kv[int(op["layer"])]
-                act[op["out"]] = attention_rows(act[op["q"]], kc, vc, int(op["H"]), int(op["Hkv"]), int(op["D"]), pos,
-                                                op["Ms"], op["Ss"], op["Mo"], op["So"], op.get("prob_bits", 8))
-            elif kind == "add":
-                act[op["out"]] = vadd(act[op["a"]], act[op["b"]], op["sh_b"])
-            elif kind == "mul":
-                act[op["out"]] = vmul(act[op["a"]], act[op["b"]], op["sh"])
-            elif kind == "silu":
-                act[op["out"]] = silu16(act[op["in"]], op["Mi"], op["Si"], op["sh_out"])
-            else:
-                raise ValueError(f"unknown qgraph op {kind!r}")
+            self.step(op, act, pos)
         if acts is not None:
             acts.update(act)
         return act[self.q.output_name]
+
+    def step(self, op, act, pos):
+        """Execute one qgraph op on the activation dict `act` (golden.py:281-312)."""
+        T = self.q.tensors
+        M = act[self.q.input_name].shape[0]
+        kind = op["op"]
+        if kind == "rmsnorm":
+            x = act[op["in"]]
+            g = T[op["gamma"]]
+            heads = int(op.get("heads", 1))
+            if heads < 1 or x.shape[1] != heads * len(g):
+                raise ValueError("RMSNorm head geometry mismatch")
+            y = rmsnorm(x.reshape(-1, len(g)), g, op["eps_t"], op["C"], op["sh_post"])
+            act[op["out"]] = y.reshape(x.shape)
+        elif kind == "quant":
+            act[op["out"]] = vquant(act[op["in"]], op["M"], op["S"])
+        elif kind == "linear":
+            act[op["out"]] = self._linear(op, act)
+        elif kind == "linear_partial":
+            # tensor parallel: this rank's K slice of a row-split linear, raw int32 sums
+            a, w = act[op["in"]], T[op["w"]]
+            if w.shape != (int(op["N"]), int(op["K"])) or a.shape[1] != int(op["K"]):
+                raise ValueError(f"linear_partial {op['out']}: shape mismatch")
+            acc = exact_matmul(a, w)
+            if np.abs(acc).max(initial=0) >= 2**31:
+                raise ValueError("int32 partial accumulator overflow")
+            act[op["out"]] = acc
+        elif kind == "requant":
+            # tensor parallel: bias + requant + epilogue of the all-reduced accumulator
+            act[op["out"]] = self._requant(op, act[op["in"]], act)
+        elif kind == "allreduce":
+            raise ValueError("allreduce needs the other ranks: run the graph with a tensor-parallel runner")
+        elif kind == "rope":
+            act[op["out"]] = rope(act[op["in"]], int(op["H"]), int(op["D"]), self.rope_cos, self.rope_sin, pos)
+        elif kind == "kv_write":
+            kc, vc = self.kv[int(op["layer"])]
+            Hkv, D = int(op["Hkv"]), int(op["D"])
+            k = act[op["k"]].reshape(M, Hkv, D)
+            v = act[op["v"]].reshape(M, Hkv, D)
+            kc[:, pos : pos + M] = k.transpose(1, 0, 2)
+            vc[:, pos : pos + M] = v.transpose(1, 0, 2)
+        elif kind == "attention":
+            kc, vc = self.kv[int(op["layer"])]
+            act[op["out"]] = attention_rows(act[op["q"]], kc, vc, int(op["H"]), int(op["Hkv"]), int(op["D"]), pos,
+                                            op["Ms"], op["Ss"], op["Mo"], op["So"], op.get("prob_bits", 8))
+        elif kind == "add":
+            act[op["out"]] = vadd(act[op["a"]], act[op["b"]], op["sh_b"])
+        elif kind == "mul":
+            act[op["out"]] = vmul(act[op["a"]], act[op["b"]], op["sh"])
+        elif kind == "silu":
+            act[op["out"]] = silu16(act[op["in"]], op["Mi"], op["Si"], op["sh_out"])
+        else:
+            raise ValueError(f"unknown qgraph op {kind!r}")
 
     def embed_rows(self, tokens, M):
         rows = np.zeros((M, self.dim), I64)
