@@ -139,8 +139,6 @@ __device__ __forceinline__ uint4 dsmem_ld4(const void* local, uint32_t rank) {
 }
 
 __device__ __forceinline__ int64_t rshr64(int64_t v, int s) { return s == 0 ? v : (v >> s) + ((v >> (s - 1)) & 1); }
-__device__ __forceinline__ int32_t sat16_64(int64_t v) { return (int32_t)(v < -32768 ? -32768 : (v > 32767 ? 32767 : v)); }
-__device__ __forceinline__ int32_t sat8_64(int64_t v) { return (int32_t)(v < -128 ? -128 : (v > 127 ? 127 : v)); }
 __device__ __forceinline__ int32_t sat16_32(int32_t v) { return v < -32768 ? -32768 : (v > 32767 ? 32767 : v); }
 // rshr of a value with |v| < 2^31: 32-bit arithmetic for s < 31, 64-bit otherwise
 __device__ __forceinline__ int32_t rshr_small(int32_t v, int s) {
@@ -149,17 +147,25 @@ __device__ __forceinline__ int32_t rshr_small(int32_t v, int s) {
   return (int32_t)rshr64(v, s);
 }
 
-// Per-channel requant of an int32 accumulator (NUMERICS.md:69-71): v = acc + bias in 64 bits
-// (or 32 when the host proved |acc + bias| < 2^31), times M (< 2^32) in 64 bits, rshr S.
-__device__ __forceinline__ int64_t requant64(int32_t acc, int64_t bias, uint32_t M, int S, bool narrow) {
+// Per-channel requant of an int32 accumulator (NUMERICS.md:69-71) saturated to [lo, hi]:
+// v = acc + bias in 32 bits when the host proved |acc + bias| < 2^31 (narrow), else in 64;
+// v * M (M < 2^32) in 64 bits, rshr S.  Straight-line code: the 16 channels of a chunk
+// interleave freely.
+__device__ __forceinline__ int32_t requant_sat(int32_t acc, int64_t bias, uint32_t M, int S, bool narrow, int32_t lo,
+                                               int32_t hi) {
   const int64_t v = narrow ? (int64_t)(int32_t)(acc + (int32_t)bias) : (int64_t)acc + bias;
-  return rshr64(narrow ? (int64_t)(int32_t)v * (int64_t)M : (int64_t)((uint64_t)v * (uint64_t)M), S);
+  const int64_t t = rshr64(narrow ? (int64_t)(int32_t)v * (int64_t)M : (int64_t)((uint64_t)v * (uint64_t)M), S);
+  return (int32_t)(t < lo ? lo : (t > hi ? hi : t));
+}
+__device__ __forceinline__ int32_t mulshift_clamp(int32_t v, uint32_t M, int S, int32_t lo, int32_t hi) {
+  const int64_t t = rshr64((int64_t)v * (int64_t)M, S);
+  return (int32_t)(t < lo ? lo : (t > hi ? hi : t));
 }
 
 // SiLU of an i16 value with the sigmoid table in shared memory (numerics.h:45-51).  Every
 // intermediate after the input scaling fits 32 bits: |x * sg| <= 2^15 * 65514 < 2^31.
 __device__ __forceinline__ int32_t silu_fast(int32_t x, uint32_t Mi, int Si, int sh_out, const uint16_t* sig) {
-  const int32_t u = sat16_64(rshr64((int64_t)x * (int64_t)Mi, Si));
+  const int32_t u = mulshift_clamp(x, Mi, Si, -32768, 32767);
   const int idx = (u >> 8) + 128;
   const int32_t f = u & 255;
   const int32_t lo = sig[idx];
@@ -181,7 +187,9 @@ __device__ __forceinline__ void store16_i16(int16_t* p, const int32_t* o, int cn
     reinterpret_cast<uint4*>(p)[0] = w0;
     reinterpret_cast<uint4*>(p)[1] = w1;
   } else {
-    for (int j = 0; j < cnt; ++j) p[j] = (int16_t)o[j];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < cnt) p[j] = (int16_t)o[j];
   }
 }
 __device__ __forceinline__ void store16_i8(int8_t* p, const int32_t* o, int cnt) {
@@ -197,7 +205,9 @@ __device__ __forceinline__ void store16_i8(int8_t* p, const int32_t* o, int cnt)
           (uint32_t)(uint8_t)o[15] << 24;
     *reinterpret_cast<uint4*>(p) = w;
   } else {
-    for (int j = 0; j < cnt; ++j) p[j] = (int8_t)o[j];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < cnt) p[j] = (int8_t)o[j];
   }
 }
 __device__ __forceinline__ void load16_i16(const int16_t* p, int32_t* v, int cnt) {
@@ -425,11 +435,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint32_t Mi = (uint32_t)a.silu_Mi;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const int32_t tg = sat16_64(requant64(ag[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], narrow));
-          const int32_t tu = sat16_64(requant64(au[j], s_bias[c0 + 16 + j], s_M[c0 + 16 + j], s_S[c0 + 16 + j], narrow));
+          const int32_t tg = requant_sat(ag[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], narrow, -32768, 32767);
+          const int32_t tu =
+              requant_sat(au[j], s_bias[c0 + 16 + j], s_M[c0 + 16 + j], s_S[c0 + 16 + j], narrow, -32768, 32767);
           sg[j] = silu_fast(tg, Mi, a.silu_Si, a.silu_sh, s_sig);
           f[j] = sat16_32(rshr_small(tu * sg[j], a.aux_shift));
-          fq[j] = sat8_64(rshr64((int64_t)f[j] * a.q_M, a.q_S));
+          fq[j] = mulshift_clamp(f[j], (uint32_t)a.q_M, a.q_S, -128, 127);
         }
         const int64_t off = (int64_t)r * a.Nout + ob;
         if (a.g_out) store16_i16(a.g_out + off, sg, cnt);
@@ -468,19 +479,23 @@ __global__ void __launch_bounds__(kThreads, 2)
               reinterpret_cast<uint4*>(p)[k] = make_uint4((uint32_t)acc[4 * k], (uint32_t)acc[4 * k + 1],
                                                           (uint32_t)acc[4 * k + 2], (uint32_t)acc[4 * k + 3]);
           } else {
-            for (int j = 0; j < cnt; ++j) p[j] = acc[j];
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (j < cnt) p[j] = acc[j];
           }
           continue;
         }
         int32_t o[16];
         if (i8) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) o[j] = sat8_64(requant64(acc[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], narrow));
+          for (int j = 0; j < 16; ++j)
+            o[j] = requant_sat(acc[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], narrow, -128, 127);
           store16_i8(reinterpret_cast<int8_t*>(dst) + (int64_t)r * ld + col, o, cnt);
           continue;
         }
 #pragma unroll
-        for (int j = 0; j < 16; ++j) o[j] = sat16_64(requant64(acc[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], narrow));
+        for (int j = 0; j < 16; ++j)
+          o[j] = requant_sat(acc[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], narrow, -32768, 32767);
         if (a.epi == EPI_RESADD || a.epi == EPI_MUL) {
           int32_t aux[16];
           load16_i16(a.aux + (int64_t)r * a.N + nb, aux, cnt);

@@ -150,5 +150,8 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st);
 cudaError_t prepare_attention(size_t smem);
 size_t attention_smem_bytes(int H, int Hkv, int D, int T);
 size_t attention_decode_smem_bytes(int H, int Hkv, int D, int max_seq);
+// measures resident clusters of the decode kernel for this geometry (after prepare_attention;
+// outside stream capture): the decode launch picks its cluster size from them
+cudaError_t prepare_attention_decode(int H, int Hkv, int D, int max_seq);
 
 }  // namespace llx

@@ -11,6 +11,9 @@
 
 #include <climits>
 #include <cstdint>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "kernels.h"
 #include "launch.cuh"
@@ -122,27 +125,46 @@ __global__ void k_attention(const int8_t* __restrict__ q, const int8_t* __restri
 }
 
 // ---------------------------------------------------------------------------------------
-// Decode attention (one query row per sequence): one CTA per (sequence, KV head) streams
-// the key rows, then the value rows, with 16-byte loads.  LPK = D/16 lanes share one key
-// row; the H/Hkv query heads of the KV head reuse every loaded row.  Per-head max / sum /
-// normalisation run one warp per head over the scores kept in shared memory; the value
-// pass accumulates RB heads at a time in registers, reduces across lanes with shuffles and
-// across warps through shared memory.  All reductions are integer: exact in any order.
+// Decode attention (one query row per sequence), split over a thread-block cluster.
+//
+// The C CTAs of a cluster share one (sequence, KV head, group of up to RB query heads) and
+// take disjoint slices of the T = pos + 1 keys.  Each CTA streams its K slice, then its V
+// slice, through a ring of shared-memory stages filled by 1-D bulk copies.  The reference's
+// global order is kept exactly with three exchanges over distributed shared memory:
+//   1. per-head score maxima of every slice -> the global max (integer max);
+//   2. per-head exp-LUT sums of every slice -> the global sum -> inv = 2^31 / sum;
+//   3. per-head partial value sums sum_t pn_t * v_t of every slice -> the total
+//      (integer sums, exact in any order); each CTA finishes 1/C of the outputs.
+// Splitting the keys shortens every CTA's serial chain (load -> scores -> max -> exp ->
+// normalise -> values) by C and spreads a layer's KV stream over C times more CTAs.
 // ---------------------------------------------------------------------------------------
 constexpr int kDecThreads = 256, kDecWarps = kDecThreads / 32;
 
-// KV tiles stream through a ring of kRing shared-memory stages by 1-D bulk copies.
+// KV tiles of 8 KB stream through a ring of kRing shared-memory stages.
 constexpr int kRing = 4;
-__host__ __device__ constexpr int dec_tile_keys(int D) { return D <= 64 ? 256 : 16384 / D; }
+__host__ __device__ constexpr int dec_tile_keys(int D) { return 8192 / D; }
 
-// heads per CTA: a KV head's H/Hkv query heads are split into groups of at most 4
-__host__ __device__ constexpr int dec_heads_per_cta(int rep) { return rep < 4 ? rep : 4; }
+// query heads per CTA: a KV head's H/Hkv query heads in groups of at most 8
+__host__ __device__ constexpr int dec_heads_per_cta(int rep) { return rep < 8 ? rep : 8; }
 
+// keys per CTA slice (capacity) for cluster size C: ceil(max_seq / C) + a zero pad entry
+__host__ __device__ constexpr int dec_slice_cap(int max_seq, int C) { return ((max_seq + C - 1) / C + 2) & ~1; }
+
+static size_t dec_smem_bytes(int RB, int D, int max_seq, int C) {
+  const size_t cap = (size_t)dec_slice_cap(max_seq, C);
+  return (size_t)kRing * dec_tile_keys(D) * D + (size_t)RB * D + (size_t)RB * cap * 4 + (size_t)RB * cap * 2 +
+         (size_t)RB * D * 4 + (size_t)kDecWarps * RB * 4 + (size_t)2 * RB * 4 + 128;
+}
+
+static int dec_rb(int rep) {
+  const int h = dec_heads_per_cta(rep);
+  return h <= 1 ? 1 : h <= 2 ? 2 : h <= 4 ? 4 : 8;
+}
+
+
+// largest dynamic shared memory any decode launch of this geometry uses (cluster size 2)
 size_t attention_decode_smem_bytes(int H, int Hkv, int D, int max_seq) {
-  const int rep = dec_heads_per_cta(H / Hkv);
-  const size_t ring = (size_t)kRing * dec_tile_keys(D) * D;
-  return ring + (size_t)rep * D + (size_t)rep * max_seq * 4 + (size_t)rep * (size_t)((max_seq + 3) & ~1) * 2 +
-         (size_t)kDecWarps * rep * D * 4 + (size_t)kDecWarps * rep * 8 + 128;
+  return dec_smem_bytes(dec_rb(H / Hkv), D, max_seq, 2);
 }
 
 __device__ __forceinline__ int dot16_i8(const uint4& a, const uint4& b, int acc) {
@@ -190,34 +212,51 @@ __device__ __forceinline__ bool att_mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+__device__ __forceinline__ uint32_t dec_cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void dec_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// 32-bit word of cluster peer `rank`'s shared memory at the address of `local` in this CTA
+__device__ __forceinline__ uint32_t dec_peer_u32(const void* local, uint32_t rank) {
+  uint32_t remote, v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(att_smem_u32(local)), "r"(rank));
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(remote) : "memory");
+  return v;
+}
+
 template <int LPK, int RB>
 __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
     const int8_t* __restrict__ q, const int8_t* __restrict__ kc, const int8_t* __restrict__ vc, int8_t* __restrict__ out,
     int H, int Hkv, int max_seq, const int* __restrict__ d_pos, int64_t Ms, int Ss, int64_t Mo, int So, int prob_bits,
-    const uint16_t* __restrict__ luts, int32_t* err) {
+    const uint16_t* __restrict__ luts, int32_t* err, int C) {
   constexpr int D = LPK * 16;
-  constexpr int KPW = 32 / LPK;  // key rows per warp per step
   constexpr int TK = dec_tile_keys(D);
+  constexpr int D4 = D / 4;  // 4-channel value units per head
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ uint16_t s_expi[16], s_expf[256];
   __shared__ __align__(8) uint64_t full_bar[kRing];
   __shared__ int s_abort;
-  __shared__ uint32_t s_inv[16];
-  // this CTA serves query heads [h0, h0 + rep) of KV head blockIdx.y
+  __shared__ int32_t s_gmax[RB];
+  __shared__ uint32_t s_inv[RB];
   const int rep_all = H / Hkv;
   const int hg0 = blockIdx.z * RB;
   const int rep = min(RB, rep_all - hg0);
-  const int pstride = (max_seq + 3) & ~1;
+  const int cap = dec_slice_cap(max_seq, C);
   int8_t* ring = reinterpret_cast<int8_t*>(smem);                        // [kRing][TK][D]
-  int8_t* q_s = ring + (size_t)kRing * TK * D;                           // [rep][D]
-  int32_t* sc = reinterpret_cast<int32_t*>(q_s + rep * D);               // [rep][max_seq] scores, then p
-  int16_t* pn16 = reinterpret_cast<int16_t*>(sc + (size_t)rep * max_seq);  // [rep][pstride] normalised p
-  int32_t* red = reinterpret_cast<int32_t*>(pn16 + (size_t)rep * pstride);  // [warps][rep][D]
-  int32_t* wmax = red + (size_t)kDecWarps * rep * D;                     // [warps][rep]
-  uint32_t* wsum = reinterpret_cast<uint32_t*>(wmax + kDecWarps * rep);  // [warps][rep]
-  const int b = blockIdx.x, kvh = blockIdx.y;
+  int8_t* q_s = ring + (size_t)kRing * TK * D;                           // [RB][D]
+  int32_t* sc = reinterpret_cast<int32_t*>(q_s + RB * D);                // [RB][cap] scores, then p
+  int16_t* pn16 = reinterpret_cast<int16_t*>(sc + (size_t)RB * cap);      // [RB][cap] normalised p
+  int32_t* opart = reinterpret_cast<int32_t*>(pn16 + (size_t)RB * cap);   // [RB][D] this slice's value sums
+  int32_t* wred = opart + RB * D;                                        // [warps][RB]
+  int32_t* xmax = wred + kDecWarps * RB;                                 // [RB] slice maxima (read by peers)
+  uint32_t* xsum = reinterpret_cast<uint32_t*>(xmax + RB);               // [RB] slice sums (read by peers)
+  const uint32_t crank = dec_cluster_rank();
+  const int b = blockIdx.x / C, kvh = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int sub = lane % LPK, kg = lane / LPK;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kRing; ++i) att_mbar_init(&full_bar[i]);
     s_abort = 0;
@@ -232,12 +271,15 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   }
   pdl_wait();  // POS, q and the KV cache come from earlier kernels
   const int T = *d_pos + 1;
-  const int ntile = (T + TK - 1) / TK;  // tiles of K, then as many of V
+  const int chunk = (T + C - 1) / C;
+  const int k0 = min(T, (int)crank * chunk), k1 = min(T, k0 + chunk);
+  const int nkeys = k1 - k0;
+  const int ntile = (nkeys + TK - 1) / TK;  // tiles of K, then as many of V
   const int8_t* kbase = kc + ((int64_t)b * Hkv + kvh) * max_seq * D;
   const int8_t* vbase = vc + ((int64_t)b * Hkv + kvh) * max_seq * D;
   auto issue = [&](int i) {  // tile i of the K-then-V sequence into stage i % kRing
     const int kv = i >= ntile, ti = kv ? i - ntile : i;
-    const int t0 = ti * TK, nk = min(TK, T - t0);
+    const int t0 = k0 + ti * TK, nk = min(TK, k1 - t0);
     att_bulk_load(ring + (size_t)(i % kRing) * TK * D, (kv ? vbase : kbase) + (int64_t)t0 * D, (uint32_t)(nk * D),
                   &full_bar[i % kRing]);
   };
@@ -247,167 +289,195 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   const int8_t* qrow = q + ((int64_t)b * H + (int64_t)kvh * rep_all + hg0) * D;
   for (int i = threadIdx.x; i < rep * D / 16; i += blockDim.x)
     reinterpret_cast<uint4*>(q_s)[i] = reinterpret_cast<const uint4*>(qrow)[i];
-
-  int32_t mxl[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) mxl[j] = INT_MIN;
-  const int pmax = (1 << prob_bits) - 1, pshift = 31 - prob_bits;
-  int32_t acc[RB][16];
-  int8_t* orow = out + ((int64_t)b * H + (int64_t)kvh * rep_all + hg0) * D;
-  {
-    const int j0 = 0;  // rep <= RB: every head of this CTA in one pass over V
-#pragma unroll
-    for (int r = 0; r < RB; ++r)
-#pragma unroll
-      for (int i = 0; i < 16; ++i) acc[r][i] = 0;
-    for (int i = 0; i < 2 * ntile; ++i) {
-      const int stage = i % kRing;
-      const uint32_t parity = (uint32_t)((i / kRing) & 1);
-      if (!att_mbar_wait(&full_bar[stage], parity)) {
-        s_abort = 1;
-        if (err) atomicExch(err, 5);
-      }
-      __syncthreads();
-      if (s_abort) break;
-      const int8_t* tile = ring + (size_t)stage * TK * D;
-      const int kv = i >= ntile, ti = kv ? i - ntile : i;
-      const int t0 = ti * TK, nk = min(TK, T - t0);
-      if (!kv) {
-        // ---- scores of this K tile (one key per lane), running per-head maxima ----
-        // lane l reads its row's 16-byte chunks starting at chunk l % LPK, so the 32 rows of a
-        // warp spread over all shared-memory banks
-        for (int l = warp * 32 + lane; l < nk; l += 32 * kDecWarps) {
-          const int8_t* krow = tile + (size_t)l * D;
-          int sv[RB];
-#pragma unroll
-          for (int r = 0; r < RB; ++r) sv[r] = 0;
-#pragma unroll
-          for (int cc = 0; cc < LPK; ++cc) {
-            const int c = (cc + l) % LPK;
-            const uint4 kk = reinterpret_cast<const uint4*>(krow)[c];
-#pragma unroll
-            for (int r = 0; r < RB; ++r) {
-              if (r < rep) sv[r] = dot16_i8(kk, reinterpret_cast<const uint4*>(q_s + r * D)[c], sv[r]);
-            }
-          }
-#pragma unroll
-          for (int r = 0; r < RB; ++r) {
-            if (r < rep) {
-              mxl[r] = max(mxl[r], sv[r]);
-              sc[r * max_seq + t0 + l] = sv[r];
-            }
-          }
-        }
-        if (i == ntile - 1) {
-          // ---- all scores are in: per-head max, exp LUT probabilities, sums, Q0.15 ----
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            if (j >= rep) break;
-            int32_t v = mxl[j];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
-            if (lane == 0) wmax[warp * rep + j] = v;
-          }
-          __syncthreads();
-          for (int j = 0; j < rep; ++j) {
-            int32_t mx = wmax[j];
-            for (int w = 1; w < kDecWarps; ++w) mx = max(mx, wmax[w * rep + j]);
-            int32_t* sj = sc + j * max_seq;
-            uint32_t sum = 0;
-            for (int t = threadIdx.x; t < T; t += blockDim.x) {
-              const uint32_t p = gap_prob((uint32_t)(mx - sj[t]), (uint32_t)Ms, Ss, s_expi, s_expf);
-              sj[t] = (int32_t)p;
-              sum += p;
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            if (lane == 0) wsum[warp * rep + j] = sum;
-          }
-          __syncthreads();
-          if (threadIdx.x < rep) {
-            // inv = udiv(2^31, sum): 2^31 fits 32 bits, so a 32-bit divide is exact
-            uint32_t sum = 0;
-            for (int w = 0; w < kDecWarps; ++w) sum += wsum[w * rep + threadIdx.x];
-            s_inv[threadIdx.x] = 0x80000000u / (sum ? sum : 1u);
-          }
-          __syncthreads();
-          for (int j = 0; j < rep; ++j) {
-            // p <= sum, so p * inv <= 2^31 - 1: the product and its rounding shift stay in 32 bits
-            const uint32_t inv = s_inv[j];
-            const int32_t* sj = sc + j * max_seq;
-            int16_t* pj = pn16 + (size_t)j * pstride;
-            for (int t = threadIdx.x; t < T + 2; t += blockDim.x) {
-              int32_t v = 0;
-              if (t < T) {
-                const uint32_t x = (uint32_t)sj[t] * inv;
-                const uint32_t pn = (x >> pshift) + ((x >> (pshift - 1)) & 1u);
-                v = (int32_t)(pn < (uint32_t)pmax ? pn : (uint32_t)pmax);
-              }
-              if (t < pstride) pj[t] = (int16_t)v;
-            }
-          }
-        }
-      } else {
-        // ---- values of this V tile: key pairs through dp2a ----
-        for (int l = (warp * KPW + kg) * 2; l < nk; l += KPW * kDecWarps * 2) {
-          const int t = t0 + l;
-          const uint4 va = reinterpret_cast<const uint4*>(tile + (size_t)l * D)[sub];
-          // the row after the last key is stale shared memory, weighted by pn = 0
-          const uint4 vb = reinterpret_cast<const uint4*>(tile + (size_t)(l + 1) * D)[sub];
-          const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
-          uint32_t x[8];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            x[2 * k] = __byte_perm(wa[k], wb[k], 0x5140);
-            x[2 * k + 1] = __byte_perm(wa[k], wb[k], 0x7362);
-          }
-#pragma unroll
-          for (int r = 0; r < RB; ++r) {
-            const int j = j0 + r;
-            if (j >= rep) break;
-            const int pp = *reinterpret_cast<const int*>(pn16 + (size_t)j * pstride + t);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              acc[r][2 * k] = __dp2a_lo(pp, (int)x[k], acc[r][2 * k]);
-              acc[r][2 * k + 1] = __dp2a_hi(pp, (int)x[k], acc[r][2 * k + 1]);
-            }
-          }
-        }
-      }
-      __syncthreads();  // stage consumed by every thread
-      if (threadIdx.x == 0 && i + kRing < 2 * ntile) issue(i + kRing);
-    }
-  }
-  if (!s_abort) {
-    const int j0 = 0;
-    // ---- reduce the value sums: lanes with the same d chunk, then warps ----
-#pragma unroll
-    for (int o = LPK; o < 32; o <<= 1)
-#pragma unroll
-      for (int r = 0; r < RB; ++r)
-#pragma unroll
-        for (int i = 0; i < 16; ++i) acc[r][i] += __shfl_xor_sync(0xffffffffu, acc[r][i], o);
-    if (kg == 0) {
-#pragma unroll
-      for (int r = 0; r < RB; ++r)
-        if (j0 + r < rep)
-#pragma unroll
-          for (int i = 0; i < 16; ++i) red[((size_t)warp * rep + j0 + r) * D + sub * 16 + i] = acc[r][i];
+  auto wait_stage = [&](int i) {
+    if (s_abort == 0 && !att_mbar_wait(&full_bar[i % kRing], (uint32_t)((i / kRing) & 1))) {
+      s_abort = 1;
+      if (err) atomicExch(err, 5);
     }
     __syncthreads();
-    for (int idx = threadIdx.x; idx < RB * D; idx += blockDim.x) {
-      const int j = j0 + idx / D, d = idx % D;
-      if (j >= rep) continue;
-      int32_t o = 0;
+    return s_abort == 0;
+  };
+
+  // ---- K slice: one key per lane, scores of every head, running per-head maxima ----
+  int32_t mxl[RB];
 #pragma unroll
-      for (int w = 0; w < kDecWarps; ++w) o += red[((size_t)w * rep + j) * D + d];
-      int64_t ov = o;
-      if (prob_bits == 15) ov = rshr(ov, 7);
-      orow[j * D + d] = (int8_t)sat8(mulshift(ov, Mo, So));
+  for (int j = 0; j < RB; ++j) mxl[j] = INT_MIN;
+  for (int i = 0; i < ntile; ++i) {
+    if (!wait_stage(i)) break;
+    const int8_t* tile = ring + (size_t)(i % kRing) * TK * D;
+    const int lt0 = i * TK, nk = min(TK, nkeys - lt0);
+    for (int l = threadIdx.x; l < nk; l += kDecThreads) {
+      const int8_t* krow = tile + (size_t)l * D;
+      int sv[RB];
+#pragma unroll
+      for (int r = 0; r < RB; ++r) sv[r] = 0;
+#pragma unroll
+      for (int cc = 0; cc < LPK; ++cc) {
+        // rotate the starting chunk by key so a warp's 32 rows spread over the banks
+        const int c = (cc + l) % LPK;
+        const uint4 kk = reinterpret_cast<const uint4*>(krow)[c];
+#pragma unroll
+        for (int r = 0; r < RB; ++r)
+          if (r < rep) sv[r] = dot16_i8(kk, reinterpret_cast<const uint4*>(q_s + r * D)[c], sv[r]);
+      }
+#pragma unroll
+      for (int r = 0; r < RB; ++r)
+        if (r < rep) {
+          mxl[r] = max(mxl[r], sv[r]);
+          sc[r * cap + lt0 + l] = sv[r];
+        }
+    }
+    __syncthreads();  // stage consumed by every thread
+    if (threadIdx.x == 0 && i + kRing < 2 * ntile) issue(i + kRing);
+  }
+  // ---- exchange 1: slice maxima -> global per-head max ----
+#pragma unroll
+  for (int j = 0; j < RB; ++j) {
+    int32_t v = mxl[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) wred[warp * RB + j] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < RB) {
+    int32_t v = INT_MIN;
+    for (int w = 0; w < kDecWarps; ++w) v = max(v, wred[w * RB + threadIdx.x]);
+    xmax[threadIdx.x] = v;
+  }
+  dec_cluster_sync();
+  if (threadIdx.x < C * RB) {
+    // thread r * RB + j reads peer r's maximum of head j; the C reads run concurrently
+    const int j = threadIdx.x % RB, r = threadIdx.x / RB;
+    wred[threadIdx.x] = (int32_t)dec_peer_u32(xmax + j, (uint32_t)r);
+  }
+  __syncthreads();
+  if (threadIdx.x < rep) {
+    int32_t v = INT_MIN;
+    for (int r = 0; r < C; ++r) v = max(v, wred[r * RB + threadIdx.x]);
+    s_gmax[threadIdx.x] = v;
+  }
+  __syncthreads();
+  // ---- exp-LUT probabilities of the slice, slice sums ----
+  const bool live = s_abort == 0;
+  {
+    int32_t mx[RB];
+    uint32_t sum[RB];
+#pragma unroll
+    for (int j = 0; j < RB; ++j) {
+      mx[j] = j < rep ? s_gmax[j] : 0;
+      sum[j] = 0;
+    }
+    if (live)
+      for (int t = threadIdx.x; t < nkeys; t += kDecThreads) {
+#pragma unroll
+        for (int j = 0; j < RB; ++j) {
+          if (j < rep) {
+            const uint32_t pr = gap_prob((uint32_t)(mx[j] - sc[j * cap + t]), (uint32_t)Ms, Ss, s_expi, s_expf);
+            sc[j * cap + t] = (int32_t)pr;
+            sum[j] += pr;
+          }
+        }
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int j = 0; j < RB; ++j) sum[j] += __shfl_xor_sync(0xffffffffu, sum[j], o);
+    if (lane == 0)
+#pragma unroll
+      for (int j = 0; j < RB; ++j) wred[warp * RB + j] = (int32_t)sum[j];
+  }
+  __syncthreads();
+  if (threadIdx.x < RB) {
+    uint32_t v = 0;
+    if (threadIdx.x < rep)
+      for (int w = 0; w < kDecWarps; ++w) v += (uint32_t)wred[w * RB + threadIdx.x];
+    xsum[threadIdx.x] = v;
+  }
+  // ---- exchange 2: slice sums -> global sum -> inv = 2^31 / sum (32-bit divide, exact) ----
+  dec_cluster_sync();
+  if (threadIdx.x < C * RB) {
+    const int j = threadIdx.x % RB, r = threadIdx.x / RB;
+    wred[threadIdx.x] = (int32_t)dec_peer_u32(xsum + j, (uint32_t)r);
+  }
+  __syncthreads();
+  if (threadIdx.x < rep) {
+    uint32_t v = 0;
+    for (int r = 0; r < C; ++r) v += (uint32_t)wred[r * RB + threadIdx.x];
+    s_inv[threadIdx.x] = 0x80000000u / (v ? v : 1u);
+  }
+  __syncthreads();
+  // ---- normalised probabilities: pn = min(pmax, rshr(p * inv, 31 - prob_bits)) ----
+  // p <= sum, so p * inv <= 2^31: the product and its rounding shift stay in 32 bits
+  const uint32_t pmax = (1u << prob_bits) - 1u;
+  const int pshift = 31 - prob_bits;
+  for (int j = 0; j < rep; ++j) {
+    const uint32_t inv = s_inv[j];
+    const int32_t* sj = sc + j * cap;
+    int16_t* pj = pn16 + (size_t)j * cap;
+    for (int t = threadIdx.x; t < cap; t += kDecThreads) {
+      uint32_t v = 0;
+      if (t < nkeys && live) {
+        const uint32_t x = (uint32_t)sj[t] * inv;
+        const uint32_t pn = (x >> pshift) + ((x >> (pshift - 1)) & 1u);
+        v = pn < pmax ? pn : pmax;
+      }
+      pj[t] = (int16_t)v;  // entries past the slice stay 0: they weight the stale pair row
     }
   }
-  // drain (bounded) the copies still in flight after an abort before the CTA exits
   __syncthreads();
+  // ---- V slice: unit u = (head j, 4 channels) accumulates over the slice's keys in pairs ----
+  int32_t acc[2][4];
+#pragma unroll
+  for (int x = 0; x < 2; ++x)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[x][k] = 0;
+  const int units = rep * D4;
+  for (int i = ntile; i < 2 * ntile; ++i) {
+    if (!wait_stage(i)) break;
+    const int8_t* tile = ring + (size_t)(i % kRing) * TK * D;
+    const int lt0 = (i - ntile) * TK, nk = min(TK, nkeys - lt0);
+#pragma unroll
+    for (int x = 0; x < 2; ++x) {
+      const int u = threadIdx.x + x * kDecThreads;
+      if (u >= units) break;
+      const int j = u / D4, c4 = (u % D4) * 4;
+      const int16_t* pj = pn16 + (size_t)j * cap + lt0;
+      for (int l = 0; l < nk; l += 2) {
+        // the row after the last key may be stale shared memory: its pn is 0
+        const uint32_t va = *reinterpret_cast<const uint32_t*>(tile + (size_t)l * D + c4);
+        const uint32_t vb = *reinterpret_cast<const uint32_t*>(tile + (size_t)(l + 1) * D + c4);
+        const int pp = *reinterpret_cast<const int*>(pj + l);
+        const uint32_t lo = __byte_perm(va, vb, 0x5140), hi = __byte_perm(va, vb, 0x7362);
+        acc[x][0] = __dp2a_lo(pp, (int)lo, acc[x][0]);
+        acc[x][1] = __dp2a_hi(pp, (int)lo, acc[x][1]);
+        acc[x][2] = __dp2a_lo(pp, (int)hi, acc[x][2]);
+        acc[x][3] = __dp2a_hi(pp, (int)hi, acc[x][3]);
+      }
+    }
+    __syncthreads();  // stage consumed by every thread
+    if (threadIdx.x == 0 && i + kRing < 2 * ntile) issue(i + kRing);
+  }
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    const int u = threadIdx.x + x * kDecThreads;
+    if (u < units)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) opart[(u / D4) * D + (u % D4) * 4 + k] = acc[x][k];
+  }
+  // ---- exchange 3: slice value sums -> outputs; CTA `crank` finishes outputs idx = crank mod C ----
+  dec_cluster_sync();
+  if (s_abort == 0) {
+    int8_t* orow = out + ((int64_t)b * H + (int64_t)kvh * rep_all + hg0) * D;
+    for (int idx = (int)crank + C * threadIdx.x; idx < rep * D; idx += C * kDecThreads) {
+      int32_t o = 0;
+      for (int r = 0; r < C; ++r) o += (int32_t)dec_peer_u32(opart + idx, (uint32_t)r);
+      int64_t ov = o;
+      if (prob_bits == 15) ov = rshr(ov, 7);
+      orow[idx] = (int8_t)sat8(mulshift(ov, Mo, So));
+    }
+  }
+  dec_cluster_sync();  // peers keep their shared memory until every CTA has read it
+  // drain (bounded) the copies still in flight after an abort before the CTA exits
   if (threadIdx.x == 0 && s_abort)
     for (int i = 0; i < kRing; ++i) {
       for (uint32_t it = 0; it < (1u << 20); ++it) {
@@ -424,34 +494,438 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
     }
 }
 
+// Resident clusters per cluster size, measured with the occupancy API at model load
+// (outside any stream capture) for each decode geometry: key (LPK, RB, max_seq, C).
+static std::mutex g_occ_mu;
+static std::map<std::tuple<int, int, int, int>, int> g_occ;
+
 template <int LPK, int RB>
-static cudaError_t launch_dec_rb(const AttnArgs& a, size_t smem, cudaStream_t st) {
+static cudaError_t measure_dec_occupancy(int max_seq) {
+  for (int C = 2; C <= 8; C *= 2) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(C * 148, 1, 1);
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.dynamicSmemBytes = dec_smem_bytes(RB, LPK * 16, max_seq, C);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, k_attention_decode<LPK, RB>, &cfg);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(g_occ_mu);
+    g_occ[std::make_tuple(LPK, RB, max_seq, C)] = clusters;
+  }
+  return cudaSuccess;
+}
+
+// Cluster size: the largest C in {8, 4, 2} whose B * Hkv * groups clusters are all resident
+// at once (one wave: the slowest slice bounds the launch); 2 when no size fits in one wave.
+template <int LPK, int RB>
+static int dec_cluster_size(int units, int max_seq) {
+  std::lock_guard<std::mutex> lock(g_occ_mu);
+  for (int C = 8; C >= 2; C /= 2) {
+    auto it = g_occ.find(std::make_tuple(LPK, RB, max_seq, C));
+    if (it != g_occ.end() && it->second >= units) return C;
+  }
+  return 2;
+}
+
+template <int LPK, int RB>
+static cudaError_t launch_dec_rb(const AttnArgs& a, cudaStream_t st) {
   const int groups = (a.H / a.Hkv + RB - 1) / RB;
-  const cudaError_t e = launch_k(k_attention_decode<LPK, RB>, dim3(a.B, a.Hkv, groups), dim3(kDecThreads), smem, st, a.q, a.kc,
-                                 a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos, a.Ms, a.Ss, a.Mo, a.So, a.prob_bits,
-                                 a.luts, a.err);
+  const int C = dec_cluster_size<LPK, RB>(a.B * a.Hkv * groups, a.max_seq);
+  const size_t smem = dec_smem_bytes(RB, LPK * 16, a.max_seq, C);
+  const cudaError_t e = launch_kc(k_attention_decode<LPK, RB>, dim3(a.B * C, a.Hkv, groups), dim3(kDecThreads), smem,
+                                  st, dim3(C, 1, 1), a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos, a.Ms, a.Ss,
+                                  a.Mo, a.So, a.prob_bits, a.luts, a.err, C);
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
-// heads per CTA (and per value pass): dec_heads_per_cta
 template <int LPK>
-static cudaError_t launch_dec_l(const AttnArgs& a, size_t smem, cudaStream_t st) {
-  const int rep = a.H / a.Hkv;
-  if (rep >= 4) return launch_dec_rb<LPK, 4>(a, smem, st);
-  if (rep >= 2) return launch_dec_rb<LPK, 2>(a, smem, st);
-  return launch_dec_rb<LPK, 1>(a, smem, st);
+static cudaError_t launch_dec_l(const AttnArgs& a, cudaStream_t st) {
+  switch (dec_rb(a.H / a.Hkv)) {
+    case 1: return launch_dec_rb<LPK, 1>(a, st);
+    case 2: return launch_dec_rb<LPK, 2>(a, st);
+    case 4: return launch_dec_rb<LPK, 4>(a, st);
+    default: return launch_dec_rb<LPK, 8>(a, st);
+  }
 }
 template <int LPK>
 static cudaError_t prep_dec_l(size_t smem) {
-  for (auto f : {k_attention_decode<LPK, 1>, k_attention_decode<LPK, 2>, k_attention_decode<LPK, 4>}) {
+  for (auto f : {k_attention_decode<LPK, 1>, k_attention_decode<LPK, 2>, k_attention_decode<LPK, 4>,
+                 k_attention_decode<LPK, 8>}) {
     const cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
 }
 
+
+template <int LPK>
+static cudaError_t measure_dec_l(int rep, int max_seq) {
+  switch (dec_rb(rep)) {
+    case 1: return measure_dec_occupancy<LPK, 1>(max_seq);
+    case 2: return measure_dec_occupancy<LPK, 2>(max_seq);
+    case 4: return measure_dec_occupancy<LPK, 4>(max_seq);
+    default: return measure_dec_occupancy<LPK, 8>(max_seq);
+  }
+}
+
+cudaError_t prepare_attention_decode(int H, int Hkv, int D, int max_seq) {
+  const int rep = H / Hkv;
+  switch (D) {
+    case 16: return measure_dec_l<1>(rep, max_seq);
+    case 32: return measure_dec_l<2>(rep, max_seq);
+    case 64: return measure_dec_l<4>(rep, max_seq);
+    case 128: return measure_dec_l<8>(rep, max_seq);
+    case 256: return measure_dec_l<16>(rep, max_seq);
+    default: return cudaSuccess;
+  }
+}
+
+cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t st) {
+  if (a.B <= 0) return cudaSuccess;
+  switch (a.D) {
+    case 16: return launch_dec_l<1>(a, st);
+    case 32: return launch_dec_l<2>(a, st);
+    case 64: return launch_dec_l<4>(a, st);
+    case 128: return launch_dec_l<8>(a, st);
+    case 256: return launch_dec_l<16>(a, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Prefill attention (M > 1 query rows per sequence): int8 MMA tiles.
+//
+// A CTA of 4 warps serves one (sequence, KV head) and 64 stacked (query row, query head)
+// pairs of that KV head; each warp owns 16 of them as the M side of m16n8k32 integer MMAs.
+// Key tiles of 64 rows stream through two shared-memory stages by cp.async.  The exact
+// integer softmax keeps the reference's global order with three passes over the keys:
+//   1. S = Q K^T (s8 x s8 -> s32), masked per-row max;
+//   2. S again, p = exp-LUT(mulshift(max - s)), per-row sum -> inv = 2^31 / sum;
+//   3. S again, pn = min(pmax, rshr(p * inv, 31 - prob_bits)), then O += pn V.
+// pn (up to 15 bits) enters the MMA as two unsigned bytes, O = 256 * (hi V) + (lo V), exact
+// in int32.  The value tile is transposed in shared memory with its keys permuted so that
+// the P fragments the softmax produces in the accumulator layout are the MMA's A operand
+// directly: PV operand k = 4 t + e of a 32-key chunk is key 16 h + [2t, 2t+1, 8+2t, 9+2t][e].
+// The MMA only moves multiply-adds; the exp-LUT softmax on the CUDA cores is the cost.
+// ---------------------------------------------------------------------------------------
+constexpr int kPfThreads = 128;  // 4 warps x 16 stacked rows
+constexpr int kPfKeys = 64;      // keys per tile
+constexpr int kPfRows = 64;      // stacked (row, head) pairs per CTA
+
+template <int D>
+struct PfSmem {
+  static constexpr int kKStride = D + 16;  // padded key rows: conflict-free operand loads
+  static constexpr int kVtStride = 68;     // transposed value rows: 64 keys + 4 bytes
+  static constexpr int kK = kPfKeys * kKStride;
+  static constexpr int kV = kPfKeys * D;
+  static constexpr int kVt = D * kVtStride;
+  static constexpr int kBytes = 2 * kK + 2 * kV + kVt;
+};
+
+__device__ __forceinline__ void pf_cp16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(att_smem_u32(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void pf_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void pf_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// d += a (16x32, s8 or u8 per A_U8) x b (32x8, s8)
+template <bool A_U8>
+__device__ __forceinline__ void pf_mma(int32_t (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if (A_U8)
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <int D>
+__global__ void __launch_bounds__(kPfThreads) k_attention_prefill(
+    const int8_t* __restrict__ q, const int8_t* __restrict__ kc, const int8_t* __restrict__ vc, int8_t* __restrict__ out,
+    int M, int H, int Hkv, int max_seq, const int* __restrict__ d_pos, int64_t Ms, int Ss, int64_t Mo, int So,
+    int prob_bits, const uint16_t* __restrict__ luts) {
+  using L = PfSmem<D>;
+  constexpr int KB = D / 32;  // k-blocks of Q K^T
+  constexpr int NT = D / 8;   // 8-channel tiles of P V
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ uint16_t s_expi[16], s_expf[256];
+  int8_t* Ks = reinterpret_cast<int8_t*>(smem);
+  int8_t* Vs = Ks + 2 * L::kK;
+  int8_t* Vt = Vs + 2 * L::kV;
+  const int rep = H / Hkv;
+  const int mq = kPfRows / rep;  // query rows per CTA
+  const int b = blockIdx.z, kvh = blockIdx.y, m0 = blockIdx.x * mq;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+  pdl_trigger();
+  for (int i = threadIdx.x; i < 16 + 256; i += kPfThreads) {
+    if (i < 16)
+      s_expi[i] = luts[kLutExpI + i];
+    else
+      s_expf[i - 16] = luts[kLutExpF + i - 16];
+  }
+  pdl_wait();  // POS, q and the KV cache come from earlier kernels
+  const int pos = *d_pos;
+  // this thread's stacked rows 16 warp + g (+ 8): query row, head, validity, last visible key
+  int rm[2], rj[2], rlim[2];
+  bool rv[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int r = 16 * warp + g + 8 * i;
+    rm[i] = m0 + r / rep;
+    rj[i] = r % rep;
+    rv[i] = r < mq * rep && rm[i] < M;
+    rlim[i] = rv[i] ? pos + rm[i] : -1;
+  }
+  const int Tc = pos + min(m0 + mq, M);  // keys 0..Tc-1 are visible to some row of the CTA
+  const int nkt = (Tc + kPfKeys - 1) / kPfKeys;
+  const int8_t* kbase = kc + ((int64_t)b * Hkv + kvh) * max_seq * D;
+  const int8_t* vbase = vc + ((int64_t)b * Hkv + kvh) * max_seq * D;
+
+  // Q fragments (A of Q K^T): reg e of k-block kb is row g + 8 (e & 1), channels kb*32 + 16 (e >> 1) + 4 tig
+  uint32_t qa[KB][4];
+#pragma unroll
+  for (int kb = 0; kb < KB; ++kb)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = e & 1;
+      const int ch = kb * 32 + (e >> 1) * 16 + tig * 4;
+      qa[kb][e] = rv[i] ? *reinterpret_cast<const uint32_t*>(
+                              q + ((int64_t)(b * M + rm[i]) * H + kvh * rep + rj[i]) * D + ch)
+                        : 0u;
+    }
+
+  auto load_tile = [&](int stage, int t0, bool with_v) {
+    int8_t* kd = Ks + stage * L::kK;
+    int8_t* vd = Vs + stage * L::kV;
+    for (int i = threadIdx.x; i < kPfKeys * (D / 16); i += kPfThreads) {
+      const int key = i / (D / 16), c = (i % (D / 16)) * 16;
+      const bool ok = t0 + key < Tc;
+      const int64_t off = ok ? (int64_t)(t0 + key) * D + c : 0;
+      pf_cp16(kd + key * L::kKStride + c, kbase + off, ok);
+      if (with_v) pf_cp16(vd + key * D + c, vbase + off, ok);
+    }
+  };
+  // S for keys kc0 .. kc0 + 31 of a staged tile: s[j][e] is row g + 8 (e >> 1), key kc0 + 8 j + 2 tig + (e & 1)
+  auto qk_chunk = [&](const int8_t* kst, int kc0, int32_t (&sv)[4][4]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sv[j][e] = 0;
+      const int8_t* krow = kst + (kc0 + 8 * j + g) * L::kKStride + tig * 4;
+#pragma unroll
+      for (int kb = 0; kb < KB; ++kb)
+        pf_mma<false>(sv[j], qa[kb], *reinterpret_cast<const uint32_t*>(krow + kb * 32),
+                      *reinterpret_cast<const uint32_t*>(krow + kb * 32 + 16));
+    }
+  };
+
+  // ---- pass 1: per-row max ----
+  int32_t mx[2] = {INT_MIN, INT_MIN};
+  load_tile(0, 0, false);
+  pf_commit();
+  for (int kt = 0; kt < nkt; ++kt) {
+    if (kt + 1 < nkt) load_tile((kt + 1) & 1, (kt + 1) * kPfKeys, false);
+    pf_commit();
+    pf_wait<1>();
+    __syncthreads();
+    const int8_t* kst = Ks + (kt & 1) * L::kK;
+    for (int c2 = 0; c2 < 2; ++c2) {
+      const int kc0 = kt * kPfKeys + c2 * 32;
+      if (kc0 >= Tc) break;
+      int32_t sv[4][4];
+      qk_chunk(kst, c2 * 32, sv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = kc0 + 8 * j + 2 * tig + (e & 1);
+          if (key <= rlim[e >> 1]) mx[e >> 1] = max(mx[e >> 1], sv[j][e]);
+        }
+    }
+    __syncthreads();
+  }
+  pf_wait<0>();
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    mx[i] = max(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
+    mx[i] = max(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
+  }
+
+  // ---- pass 2: exp-LUT probabilities, per-row sum -> inv ----
+  uint32_t sum[2] = {0u, 0u};
+  __syncthreads();
+  load_tile(0, 0, false);
+  pf_commit();
+  for (int kt = 0; kt < nkt; ++kt) {
+    if (kt + 1 < nkt) load_tile((kt + 1) & 1, (kt + 1) * kPfKeys, false);
+    pf_commit();
+    pf_wait<1>();
+    __syncthreads();
+    const int8_t* kst = Ks + (kt & 1) * L::kK;
+    for (int c2 = 0; c2 < 2; ++c2) {
+      const int kc0 = kt * kPfKeys + c2 * 32;
+      if (kc0 >= Tc) break;
+      int32_t sv[4][4];
+      qk_chunk(kst, c2 * 32, sv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i = e >> 1;
+          const int key = kc0 + 8 * j + 2 * tig + (e & 1);
+          if (key <= rlim[i]) sum[i] += gap_prob((uint32_t)(mx[i] - sv[j][e]), (uint32_t)Ms, Ss, s_expi, s_expf);
+        }
+    }
+    __syncthreads();
+  }
+  pf_wait<0>();
+  uint32_t inv[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    sum[i] += __shfl_xor_sync(0xffffffffu, sum[i], 1);
+    sum[i] += __shfl_xor_sync(0xffffffffu, sum[i], 2);
+    inv[i] = 0x80000000u / (sum[i] ? sum[i] : 1u);
+  }
+
+  // ---- pass 3: normalised probabilities x V ----
+  const uint32_t pmax = (1u << prob_bits) - 1u;
+  const int pshift = 31 - prob_bits;
+  const bool two = prob_bits > 8;  // pn needs its high byte
+  int32_t o[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[n][e] = 0;
+  __syncthreads();
+  load_tile(0, 0, true);
+  pf_commit();
+  for (int kt = 0; kt < nkt; ++kt) {
+    if (kt + 1 < nkt) load_tile((kt + 1) & 1, (kt + 1) * kPfKeys, true);
+    pf_commit();
+    pf_wait<1>();
+    __syncthreads();
+    // transpose the value tile into Vt[d][k] with the PV key order: keys {2t, 2t+1, 8+2t, 9+2t}
+    // (+ 16 h + 32 c) -> k = 32 c + 16 h + 4 t + 0..3, in 4 x 4 byte blocks
+    {
+      const int8_t* vst = Vs + (kt & 1) * L::kV;
+      for (int u = threadIdx.x; u < 16 * (D / 4); u += kPfThreads) {
+        const int d0 = (u % (D / 4)) * 4, kg = u / (D / 4);  // kg = c * 8 + h * 4 + t
+        const int t = kg & 3, base = (kg >> 2) * 16;       // base = 32 c + 16 h
+        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(vst + (base + 2 * t) * D + d0);
+        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(vst + (base + 2 * t + 1) * D + d0);
+        const uint32_t w2 = *reinterpret_cast<const uint32_t*>(vst + (base + 8 + 2 * t) * D + d0);
+        const uint32_t w3 = *reinterpret_cast<const uint32_t*>(vst + (base + 9 + 2 * t) * D + d0);
+        const uint32_t x0 = __byte_perm(w0, w1, 0x5140), x1 = __byte_perm(w2, w3, 0x5140);
+        const uint32_t x2 = __byte_perm(w0, w1, 0x7362), x3 = __byte_perm(w2, w3, 0x7362);
+        int8_t* dst = Vt + d0 * L::kVtStride + base + 4 * t;
+        *reinterpret_cast<uint32_t*>(dst) = __byte_perm(x0, x1, 0x5410);
+        *reinterpret_cast<uint32_t*>(dst + L::kVtStride) = __byte_perm(x0, x1, 0x7632);
+        *reinterpret_cast<uint32_t*>(dst + 2 * L::kVtStride) = __byte_perm(x2, x3, 0x5410);
+        *reinterpret_cast<uint32_t*>(dst + 3 * L::kVtStride) = __byte_perm(x2, x3, 0x7632);
+      }
+    }
+    __syncthreads();
+    const int8_t* kst = Ks + (kt & 1) * L::kK;
+    for (int c2 = 0; c2 < 2; ++c2) {
+      const int kc0 = kt * kPfKeys + c2 * 32;
+      if (kc0 >= Tc) break;
+      int32_t sv[4][4];
+      qk_chunk(kst, c2 * 32, sv);
+      // A fragments: reg e holds row g + 8 (e & 1), S tiles 2 (e >> 1) and 2 (e >> 1) + 1
+      uint32_t plo[4], phi[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = e & 1, jb = (e >> 1) * 2;
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          const int j = jb + (x >> 1), c = 2 * i + (x & 1);
+          const int key = kc0 + 8 * j + 2 * tig + (x & 1);
+          uint32_t pn = 0;
+          if (key <= rlim[i]) {
+            const uint32_t pr = gap_prob((uint32_t)(mx[i] - sv[j][c]), (uint32_t)Ms, Ss, s_expi, s_expf);
+            const uint32_t y = pr * inv[i];  // p <= sum: p * inv <= 2^31
+            pn = (y >> pshift) + ((y >> (pshift - 1)) & 1u);
+            pn = pn < pmax ? pn : pmax;
+          }
+          lo |= (pn & 255u) << (8 * x);
+          hi |= (pn >> 8) << (8 * x);
+        }
+        plo[e] = lo;
+        phi[e] = hi;
+      }
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const int8_t* vrow = Vt + (8 * n + g) * L::kVtStride + c2 * 32 + 4 * tig;
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(vrow);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(vrow + 16);
+        int32_t tl[4] = {0, 0, 0, 0};
+        pf_mma<true>(tl, plo, b0, b1);
+        if (two) {
+          int32_t th[4] = {0, 0, 0, 0};
+          pf_mma<true>(th, phi, b0, b1);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o[n][e] += th[e] * 256 + tl[e];
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o[n][e] += tl[e];
+        }
+      }
+    }
+    __syncthreads();
+  }
+  pf_wait<0>();
+  // ---- outputs: o = rshr(acc, 7) (Q0.15), sat8(mulshift(o, Mo, So)) ----
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    if (!rv[i]) continue;
+    int8_t* orow = out + ((int64_t)(b * M + rm[i]) * H + kvh * rep + rj[i]) * D;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      int64_t v0 = o[n][2 * i], v1 = o[n][2 * i + 1];
+      if (two) {
+        v0 = rshr(v0, 7);
+        v1 = rshr(v1, 7);
+      }
+      const uint32_t b0 = (uint8_t)(int8_t)sat8(mulshift(v0, Mo, So));
+      const uint32_t b1 = (uint8_t)(int8_t)sat8(mulshift(v1, Mo, So));
+      *reinterpret_cast<uint16_t*>(orow + 8 * n + 2 * tig) = (uint16_t)(b0 | (b1 << 8));
+    }
+  }
+}
+
+template <int D>
+static cudaError_t launch_prefill_d(const AttnArgs& a, cudaStream_t st) {
+  const int rep = a.H / a.Hkv;
+  const int mq = kPfRows / rep;
+  const dim3 grid((a.M + mq - 1) / mq, a.Hkv, a.B);
+  const cudaError_t e = launch_k(k_attention_prefill<D>, grid, dim3(kPfThreads), (size_t)PfSmem<D>::kBytes, st, a.q,
+                                 a.kc, a.vc, a.out, a.M, a.H, a.Hkv, a.max_seq, a.d_pos, a.Ms, a.Ss, a.Mo, a.So,
+                                 a.prob_bits, a.luts);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
 cudaError_t prepare_attention(size_t smem) {
   cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(k_attention_prefill<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, PfSmem<64>::kBytes);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(k_attention_prefill<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, PfSmem<128>::kBytes);
   if (e != cudaSuccess) return e;
   for (auto f : {prep_dec_l<1>, prep_dec_l<2>, prep_dec_l<4>, prep_dec_l<8>, prep_dec_l<16>}) {
     e = f(smem);
@@ -460,25 +934,15 @@ cudaError_t prepare_attention(size_t smem) {
   return cudaSuccess;
 }
 
-cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t st) {
-  if (a.B <= 0) return cudaSuccess;
-
-  const size_t smem = attention_decode_smem_bytes(a.H, a.Hkv, a.D, a.max_seq);
-  switch (a.D) {
-    case 16: return launch_dec_l<1>(a, smem, st);
-    case 32: return launch_dec_l<2>(a, smem, st);
-    case 64: return launch_dec_l<4>(a, smem, st);
-    case 128: return launch_dec_l<8>(a, smem, st);
-    case 256: return launch_dec_l<16>(a, smem, st);
-    default: return cudaErrorInvalidValue;
-  }
-}
-
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st) {
   const int R = a.B * a.M;
   if (R <= 0) return cudaSuccess;
   if (a.M == 1 && (a.D == 16 || a.D == 32 || a.D == 64 || a.D == 128 || a.D == 256))
     return launch_attention_decode(a, st);
+  if (a.H / a.Hkv <= kPfRows && (a.prob_bits == 8 || a.prob_bits == 15)) {
+    if (a.D == 64) return launch_prefill_d<64>(a, st);
+    if (a.D == 128) return launch_prefill_d<128>(a, st);
+  }
   const size_t smem = attention_smem_bytes(a.H, a.Hkv, a.D, a.max_seq);
   dim3 grid(R, a.Hkv);
   { const cudaError_t e_ = launch_k(k_attention, dim3(grid), dim3(256), smem, st, a.q, a.kc, a.vc, a.out, a.M, a.H, a.Hkv, a.D, a.max_seq, a.d_pos, a.Ms, a.Ss,

@@ -805,6 +805,8 @@ static void load_model(llx_model* m, const std::string& dir) {
             "attention needs " + std::to_string(att_smem) + " B of shared memory for max_seq; the device allows " +
                 std::to_string(optin));
     LLX_CUDA(prepare_attention(att_smem));
+    for (const Step& x : m->steps)
+      if (x.kind == SK::Attention) LLX_CUDA(prepare_attention_decode(x.H, x.Hkv, x.D, m->max_seq));
   }
 }
 

@@ -100,7 +100,8 @@ def build(out: Path, *, dim=64, n_layers=2, H=4, Hkv=2, D=32, ffn=96, vocab=40, 
                     "Ms": int(rng.integers(1 << 30, 1 << 31)), "Ss": int(rng.integers(33, 41)),
                     "Mo": int(rng.integers(1 << 30, 1 << 31)), "So": int(rng.integers(36, 40)),
                     "prob_bits": prob_bits})
-        silu = {"Mi": 1 << 30, "Si": int(rng.integers(28, 33)), "sh_out": int(rng.integers(14, 19))}
+        silu = {"Mi": int(rng.integers(1 << 30, 1 << 32)), "Si": int(rng.integers(28, 38)),
+                "sh_out": int(rng.integers(14, 19))}
         sh_mul = int(rng.integers(12, 17))
         if fuse:
             lin(f"{p}.a", f"{p}_wo", f"{p}.x1", dim, H * D, ep="resadd", aux=resid)
