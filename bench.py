@@ -348,12 +348,15 @@ _KERNEL_OF = {"linear": "k_linear_tc", "linear_group": "k_linear_tc", "gated": "
               "requant": "k_requant", "allreduce": "ncclAllReduce"}
 
 
-def _by_kernel(prof: list[dict]) -> dict:
-    """Per-kernel-function totals of one decode launch: launches, ms, algorithmic bytes."""
+def _by_kernel(prof: list[dict], rows: int) -> dict:
+    """Per-kernel-function totals of one decode launch of `rows` rows: launches, ms,
+    algorithmic bytes.  Below 16 rows the linears run on the CUDA-core GEMV kernel."""
     out: dict[str, dict] = {}
     for p in prof:
         kind = p["label"].partition(":")[0]
         k = _KERNEL_OF.get(kind, kind)
+        if k == "k_linear_tc" and rows < 16:
+            k = "k_gemv"
         e = out.setdefault(k, {"n": 0, "ms": 0.0, "bytes": 0.0})
         e["n"] += 1
         e["ms"] += p["ms"]
@@ -498,7 +501,7 @@ def run_ours(args, dist: Dist) -> None:
     prof = m0.profile_decode(pos_mid, iters=20)
     launches_per_step = m0.decode_launches_per_step()
     step_ms_sum = sum(p["ms"] for p in prof)
-    kern = _by_kernel(prof)
+    kern = _by_kernel(prof, B // lanes)
     dom_name = max(kern, key=lambda k: kern[k]["ms"])
     dom = kern[dom_name]
     peaks = {}

@@ -56,12 +56,12 @@ cudaError_t launch_mul(const int16_t* a, const int16_t* b, int16_t* y, int64_t n
 cudaError_t launch_silu(const int16_t* x, int16_t* y, int64_t n, int64_t Mi, int Si, int sh_out,
                         const uint16_t* luts, cudaStream_t st);
 
-// logits [R][ld] i16 -> argmax over the first `vocab` entries (lowest index on ties).
-// With `keys` non-null the row's packed key (logit + 32768) << 32 | (0xFFFFFFFF - (base + n))
-// goes to keys[r] instead (a vocabulary shard starting at global channel `base`; the max of
-// the shards' keys is the global argmax), and `out` is not written.
-cudaError_t launch_argmax(const int16_t* logits, int R, int ld, int vocab, int base, int32_t* out,
-                          unsigned long long* keys, cudaStream_t st);
+// Packed argmax keys of logits [R][ld] i16 over the first `vocab` entries: keys[r] =
+// max(keys[r], max_n (logit + 32768) << 32 | (0xFFFFFFFF - (base + n))), keys zeroed by the
+// caller beforehand (base: global index of channel 0 of a vocabulary shard).  The max key
+// is the first maximum; launch_amax_finish decodes it.
+cudaError_t launch_argmax(const int16_t* logits, int R, int ld, int vocab, int base, unsigned long long* keys,
+                          cudaStream_t st);
 
 // dst[i][:] = src[idx[i]][:] for i < n (row bytes multiple of 16)
 cudaError_t launch_gather_rows(const void* src, void* dst, const int32_t* idx, int n, int row_bytes,

@@ -186,6 +186,16 @@ __device__ __forceinline__ uint32_t gap_prob(uint32_t d, uint32_t Ms, int Ss, co
   const uint32_t zi = (uint32_t)z;
   return ((uint32_t)expi[zi >> 8] * (uint32_t)expf[zi & 255] + (1u << 15)) >> 16;
 }
+// gap_prob for Ss >= 33: z = rshr(d * Ms, Ss) from the high word of the product alone,
+// z = (hi + 2^(Ss-33)) >> (Ss-32): the rounding constant leaves the low word untouched and
+// the low word adds a fraction below one, which cannot change the floor.  d < 2^23 and
+// Ms < 2^32 keep hi below 2^23.  rnd = 2^(Ss-33), sh = Ss - 32.
+__device__ __forceinline__ uint32_t gap_prob_hi(uint32_t d, uint32_t Ms, uint32_t rnd, int sh, const uint16_t* expi,
+                                                const uint16_t* expf) {
+  const uint32_t z = (__umulhi(d, Ms) + rnd) >> sh;
+  if (z >= 4096u) return 0;
+  return ((uint32_t)expi[z >> 8] * (uint32_t)expf[z & 255] + (1u << 15)) >> 16;
+}
 __device__ __forceinline__ void att_mbar_init(uint64_t* bar) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(att_smem_u32(bar)));
 }
@@ -654,7 +664,7 @@ __device__ __forceinline__ void pf_mma(int32_t (&d)[4], const uint32_t (&a)[4], 
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-template <int D>
+template <int D, bool FAST>
 __global__ void __launch_bounds__(kPfThreads) k_attention_prefill(
     const int8_t* __restrict__ q, const int8_t* __restrict__ kc, const int8_t* __restrict__ vc, int8_t* __restrict__ out,
     int M, int H, int Hkv, int max_seq, const int* __restrict__ d_pos, int64_t Ms, int Ss, int64_t Mo, int So,
@@ -692,6 +702,13 @@ __global__ void __launch_bounds__(kPfThreads) k_attention_prefill(
     rlim[i] = rv[i] ? pos + rm[i] : -1;
   }
   const int Tc = pos + min(m0 + mq, M);  // keys 0..Tc-1 are visible to some row of the CTA
+  // exp-LUT probability of a score gap (FAST: Ss >= 33, the product's high word decides z)
+  const uint32_t rnd = FAST ? 1u << (Ss - 33) : 0u;
+  const int zsh = FAST ? Ss - 32 : 0;
+  auto prob = [&](uint32_t d) {
+    return FAST ? gap_prob_hi(d, (uint32_t)Ms, rnd, zsh, s_expi, s_expf)
+                : gap_prob(d, (uint32_t)Ms, Ss, s_expi, s_expf);
+  };
   const int nkt = (Tc + kPfKeys - 1) / kPfKeys;
   const int8_t* kbase = kc + ((int64_t)b * Hkv + kvh) * max_seq * D;
   const int8_t* vbase = vc + ((int64_t)b * Hkv + kvh) * max_seq * D;
@@ -788,7 +805,7 @@ __global__ void __launch_bounds__(kPfThreads) k_attention_prefill(
         for (int e = 0; e < 4; ++e) {
           const int i = e >> 1;
           const int key = kc0 + 8 * j + 2 * tig + (e & 1);
-          if (key <= rlim[i]) sum[i] += gap_prob((uint32_t)(mx[i] - sv[j][e]), (uint32_t)Ms, Ss, s_expi, s_expf);
+          if (key <= rlim[i]) sum[i] += prob((uint32_t)(mx[i] - sv[j][e]));
         }
     }
     __syncthreads();
@@ -858,8 +875,7 @@ __global__ void __launch_bounds__(kPfThreads) k_attention_prefill(
           const int key = kc0 + 8 * j + 2 * tig + (x & 1);
           uint32_t pn = 0;
           if (key <= rlim[i]) {
-            const uint32_t pr = gap_prob((uint32_t)(mx[i] - sv[j][c]), (uint32_t)Ms, Ss, s_expi, s_expf);
-            const uint32_t y = pr * inv[i];  // p <= sum: p * inv <= 2^31
+            const uint32_t y = prob((uint32_t)(mx[i] - sv[j][c])) * inv[i];  // p <= sum: p * inv <= 2^31
             pn = (y >> pshift) + ((y >> (pshift - 1)) & 1u);
             pn = pn < pmax ? pn : pmax;
           }
@@ -914,7 +930,8 @@ static cudaError_t launch_prefill_d(const AttnArgs& a, cudaStream_t st) {
   const int rep = a.H / a.Hkv;
   const int mq = kPfRows / rep;
   const dim3 grid((a.M + mq - 1) / mq, a.Hkv, a.B);
-  const cudaError_t e = launch_k(k_attention_prefill<D>, grid, dim3(kPfThreads), (size_t)PfSmem<D>::kBytes, st, a.q,
+  auto kern = a.Ss >= 33 ? k_attention_prefill<D, true> : k_attention_prefill<D, false>;
+  const cudaError_t e = launch_k(kern, grid, dim3(kPfThreads), (size_t)PfSmem<D>::kBytes, st, a.q,
                                  a.kc, a.vc, a.out, a.M, a.H, a.Hkv, a.max_seq, a.d_pos, a.Ms, a.Ss, a.Mo, a.So,
                                  a.prob_bits, a.luts);
   return e != cudaSuccess ? e : cudaGetLastError();
@@ -923,10 +940,14 @@ static cudaError_t launch_prefill_d(const AttnArgs& a, cudaStream_t st) {
 cudaError_t prepare_attention(size_t smem) {
   cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(k_attention_prefill<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, PfSmem<64>::kBytes);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(k_attention_prefill<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, PfSmem<128>::kBytes);
-  if (e != cudaSuccess) return e;
+  for (auto f : {k_attention_prefill<64, false>, k_attention_prefill<64, true>}) {
+    e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, PfSmem<64>::kBytes);
+    if (e != cudaSuccess) return e;
+  }
+  for (auto f : {k_attention_prefill<128, false>, k_attention_prefill<128, true>}) {
+    e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, PfSmem<128>::kBytes);
+    if (e != cudaSuccess) return e;
+  }
   for (auto f : {prep_dec_l<1>, prep_dec_l<2>, prep_dec_l<4>, prep_dec_l<8>, prep_dec_l<16>}) {
     e = f(smem);
     if (e != cudaSuccess) return e;

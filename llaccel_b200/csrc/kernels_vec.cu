@@ -132,9 +132,65 @@ __global__ void k_rmsnorm(const int16_t* __restrict__ x, const int16_t* __restri
   }
 }
 
+// Wide rows (K >= 2048, e.g. Llama-3-8B's 4096): one 256-thread block per row, so a small
+// batch still spreads its rows' sums over many SMs.  Same arithmetic as k_rmsnorm.
+__global__ void k_rmsnorm_wide(const int16_t* __restrict__ x, const int16_t* __restrict__ gamma,
+                               int16_t* __restrict__ y, int8_t* __restrict__ y8, int K, int64_t eps_t, int64_t C,
+                               int sh_post, int64_t Mq, int Sq) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ uint64_t part[8];
+  __shared__ uint32_t s_inv;
+  const int row = blockIdx.x, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)row * K);
+  const uint4* gr = reinterpret_cast<const uint4*>(gamma);
+  const int chunks = K / 8;
+  uint64_t ss = 0;
+  for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+    int32_t v[8];
+    unpack8(xr[c], v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += (uint64_t)((int64_t)v[i] * v[i]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) part[w] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint64_t t = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += part[i];
+    const uint32_t r = isqrt48(t + (uint64_t)eps_t);
+    uint64_t inv = udiv((uint64_t)C, r > 1 ? r : 1);
+    s_inv = (uint32_t)(inv > 65535 ? 65535 : inv);
+  }
+  __syncthreads();
+  const int64_t inv = s_inv;
+  uint4* yr = reinterpret_cast<uint4*>(y + (int64_t)row * K);
+  uint2* yq = y8 ? reinterpret_cast<uint2*>(y8 + (int64_t)row * K) : nullptr;
+  for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+    int32_t v[8], g[8], o[8];
+    unpack8(xr[c], v);
+    unpack8(gr[c], g);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = (int32_t)sat16(rshr((int64_t)v[i] * g[i] * inv, sh_post));
+    yr[c] = pack8(o);
+    if (yq) {
+      int32_t q[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) q[i] = (int32_t)sat8(mulshift(o[i], Mq, Sq));
+      yq[c] = pack8_i8(q);
+    }
+  }
+}
+
 cudaError_t launch_rmsnorm(const int16_t* x, const int16_t* gamma, int16_t* y, int8_t* y8, int nrows, int K,
                            int64_t eps_t, int64_t C, int sh_post, int64_t Mq, int Sq, cudaStream_t st) {
   if (nrows <= 0) return cudaSuccess;
+  if (K >= 2048) {
+    const cudaError_t e = launch_k(k_rmsnorm_wide, dim3(nrows), dim3(256), 0, st, x, gamma, y, y8, K, eps_t, C,
+                                   sh_post, Mq, Sq);
+    return e != cudaSuccess ? e : cudaGetLastError();
+  }
   const int warps_per_block = 4;
   { const cudaError_t e_ = launch_k(k_rmsnorm, dim3(grid1d(nrows, warps_per_block)), dim3(32 * warps_per_block), 0, st, x, gamma, y, y8, nrows, K, eps_t, C,
                                                                              sh_post, Mq, Sq); if (e_ != cudaSuccess) return e_; }
@@ -364,15 +420,18 @@ cudaError_t launch_silu(const int16_t* x, int16_t* y, int64_t n, int64_t Mi, int
 }
 
 // ---- argmax over the first `vocab` logits, lowest index on ties (NUMERICS.md:207-208) --------
-__global__ void k_argmax(const int16_t* __restrict__ logits, int ld, int vocab, int base, int32_t* __restrict__ out,
+// Grid (rows, slices): each block takes one slice of a row's first `vocab` logits and folds
+// its best packed key (logit + 32768) << 32 | (0xFFFFFFFF - (base + n)) into keys[r] with a
+// 64-bit atomicMax (keys zeroed beforehand); the max key is the row's first maximum.
+__global__ void k_argmax(const int16_t* __restrict__ logits, int ld, int vocab, int base, int slice,
                          unsigned long long* __restrict__ keys) {
   pdl_trigger();
   pdl_wait();
   const int r = blockIdx.x;
   const int16_t* row = logits + (int64_t)r * ld;
-  // key: value in the high half, inverted global index in the low half -> max key = first max
+  const int n0 = blockIdx.y * slice, n1 = min(vocab, n0 + slice);
   unsigned long long best = 0;
-  for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+  for (int i = n0 + threadIdx.x; i < n1; i += blockDim.x) {
     const unsigned long long key =
         ((unsigned long long)(uint32_t)((int32_t)row[i] + 32768) << 32) | (0xFFFFFFFFu - (uint32_t)(base + i));
     best = key > best ? key : best;
@@ -394,19 +453,16 @@ __global__ void k_argmax(const int16_t* __restrict__ logits, int ld, int vocab, 
       const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
       best = other > best ? other : best;
     }
-    if (lane == 0) {
-      if (keys)
-        keys[r] = best;
-      else
-        out[r] = (int32_t)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
-    }
+    if (lane == 0 && best) atomicMax(keys + r, best);
   }
 }
 
-cudaError_t launch_argmax(const int16_t* logits, int R, int ld, int vocab, int base, int32_t* out,
-                          unsigned long long* keys, cudaStream_t st) {
-  if (R <= 0) return cudaSuccess;
-  { const cudaError_t e_ = launch_k(k_argmax, dim3(R), dim3(512), 0, st, logits, ld, vocab, base, out, keys); if (e_ != cudaSuccess) return e_; }
+cudaError_t launch_argmax(const int16_t* logits, int R, int ld, int vocab, int base, unsigned long long* keys,
+                          cudaStream_t st) {
+  if (R <= 0 || vocab <= 0) return cudaSuccess;
+  const int slice = 8192;
+  const dim3 grid(R, (vocab + slice - 1) / slice);
+  { const cudaError_t e_ = launch_k(k_argmax, grid, dim3(256), 0, st, logits, ld, vocab, base, slice, keys); if (e_ != cudaSuccess) return e_; }
   return cudaGetLastError();
 }
 

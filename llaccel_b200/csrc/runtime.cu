@@ -956,20 +956,15 @@ static void launch_output_argmax(llx_session* s, const void* logits, int R) {
   const llx_model* m = s->m;
   const bool fused = output_argmax_fused(m, R);
   cudaError_t e = cudaSuccess;
-  if (m->tp) {
-    if (!fused)
-      e = launch_argmax((const int16_t*)logits, R, m->vocab_padded, local_vocab(m), m->vocab_base, nullptr,
-                        s->d_amax_key, s->st);
-    if (e == cudaSuccess) {
-      std::string err;
-      tp_check(tp_allreduce_max_u64(m->tp, s->d_amax_key, R, s->st, &err), err);
-      e = launch_amax_finish(s->d_amax_key, s->d_argmax, R, s->st);
-    }
-  } else if (fused) {
-    e = launch_amax_finish(s->d_amax_key, s->d_argmax, R, s->st);
-  } else {
-    e = launch_argmax((const int16_t*)logits, R, m->vocab_padded, m->vocab, 0, s->d_argmax, nullptr, s->st);
+  // keys were zeroed by the launch's embed step (or by llx_run_rows)
+  if (!fused)
+    e = launch_argmax((const int16_t*)logits, R, m->vocab_padded, local_vocab(m), m->vocab_base, s->d_amax_key,
+                      s->st);
+  if (e == cudaSuccess && m->tp) {
+    std::string err;
+    tp_check(tp_allreduce_max_u64(m->tp, s->d_amax_key, R, s->st, &err), err);
   }
+  if (e == cudaSuccess) e = launch_amax_finish(s->d_amax_key, s->d_argmax, R, s->st);
   if (e != cudaSuccess) throw Error(LLX_ERR_CUDA, std::string("argmax launch failed: ") + cudaGetErrorString(e));
 }
 

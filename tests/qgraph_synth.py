@@ -97,7 +97,7 @@ def build(out: Path, *, dim=64, n_layers=2, H=4, Hkv=2, D=32, ffn=96, vocab=40, 
         qq, kq = quant(f"{p}.qr"), quant(f"{p}.kr")
         ops.append({"op": "kv_write", "layer": i, "k": kq, "v": f"{p}.v", "Hkv": Hkv, "D": D})
         ops.append({"op": "attention", "q": qq, "layer": i, "out": f"{p}.a", "H": H, "Hkv": Hkv, "D": D,
-                    "Ms": int(rng.integers(1 << 30, 1 << 31)), "Ss": int(rng.integers(33, 41)),
+                    "Ms": int(rng.integers(1 << 30, 1 << 31)), "Ss": int(rng.integers(28, 41)),
                     "Mo": int(rng.integers(1 << 30, 1 << 31)), "So": int(rng.integers(36, 40)),
                     "prob_bits": prob_bits})
         silu = {"Mi": int(rng.integers(1 << 30, 1 << 32)), "Si": int(rng.integers(28, 38)),
