@@ -109,15 +109,6 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* v) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
-      "[%16];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -173,56 +164,178 @@ __device__ __forceinline__ int32_t silu_fast(int32_t x, uint32_t Mi, int Si, int
   return sat16_32(rshr_small(x * sg, sh_out));
 }
 
-__device__ __forceinline__ void store16_i16(int16_t* p, const int32_t* o, int cnt) {
-  if (cnt == 16) {
-    uint4 w0, w1;
-    w0.x = (uint32_t)(uint16_t)o[0] | (uint32_t)(uint16_t)o[1] << 16;
-    w0.y = (uint32_t)(uint16_t)o[2] | (uint32_t)(uint16_t)o[3] << 16;
-    w0.z = (uint32_t)(uint16_t)o[4] | (uint32_t)(uint16_t)o[5] << 16;
-    w0.w = (uint32_t)(uint16_t)o[6] | (uint32_t)(uint16_t)o[7] << 16;
-    w1.x = (uint32_t)(uint16_t)o[8] | (uint32_t)(uint16_t)o[9] << 16;
-    w1.y = (uint32_t)(uint16_t)o[10] | (uint32_t)(uint16_t)o[11] << 16;
-    w1.z = (uint32_t)(uint16_t)o[12] | (uint32_t)(uint16_t)o[13] << 16;
-    w1.w = (uint32_t)(uint16_t)o[14] | (uint32_t)(uint16_t)o[15] << 16;
-    reinterpret_cast<uint4*>(p)[0] = w0;
-    reinterpret_cast<uint4*>(p)[1] = w1;
-  } else {
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (j < cnt) p[j] = (int16_t)o[j];
-  }
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void store16_i8(int8_t* p, const int32_t* o, int cnt) {
-  if (cnt == 16) {
-    uint4 w;
-    w.x = (uint32_t)(uint8_t)o[0] | (uint32_t)(uint8_t)o[1] << 8 | (uint32_t)(uint8_t)o[2] << 16 |
-          (uint32_t)(uint8_t)o[3] << 24;
-    w.y = (uint32_t)(uint8_t)o[4] | (uint32_t)(uint8_t)o[5] << 8 | (uint32_t)(uint8_t)o[6] << 16 |
-          (uint32_t)(uint8_t)o[7] << 24;
-    w.z = (uint32_t)(uint8_t)o[8] | (uint32_t)(uint8_t)o[9] << 8 | (uint32_t)(uint8_t)o[10] << 16 |
-          (uint32_t)(uint8_t)o[11] << 24;
-    w.w = (uint32_t)(uint8_t)o[12] | (uint32_t)(uint8_t)o[13] << 8 | (uint32_t)(uint8_t)o[14] << 16 |
-          (uint32_t)(uint8_t)o[15] << 24;
-    *reinterpret_cast<uint4*>(p) = w;
-  } else {
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (j < cnt) p[j] = (int8_t)o[j];
-  }
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t* v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void load16_i16(const int16_t* p, int32_t* v, int cnt) {
-  if (cnt == 16) {
-    const uint4 u0 = reinterpret_cast<const uint4*>(p)[0], u1 = reinterpret_cast<const uint4*>(p)[1];
-    const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+
+// UW accumulators of tile columns c0 .. c0+UW-1 for one row: from TMEM, or (split-K) the
+// sum of every cluster CTA's staged partial (integer addition: exact in any order)
+template <int UW>
+__device__ __forceinline__ void epi_fetch(int32_t (&acc)[UW], uint32_t trow, const uint4* part4, int row, int c0,
+                                          int ksplit, int nkb) {
+  if (ksplit == 1) {
+    uint32_t v[UW];
+    if (UW == 8)
+      tmem_ld8(trow + c0, v);
+    else
+      tmem_ld4(trow + c0, v);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      v[2 * j] = (int16_t)(w[j] & 0xFFFF);
-      v[2 * j + 1] = (int16_t)(w[j] >> 16);
+    for (int j = 0; j < UW; ++j) acc[j] = nkb > 0 ? (int32_t)v[j] : 0;
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < UW; ++j) acc[j] = 0;
+  for (uint32_t p = 0; p < (uint32_t)ksplit; ++p) {
+#pragma unroll
+    for (int k = 0; k < UW / 4; ++k) {
+      const uint4 v = dsmem_ld4(part4 + (c0 / 4 + k) * BM + row, p);
+      acc[4 * k] += (int32_t)v.x;
+      acc[4 * k + 1] += (int32_t)v.y;
+      acc[4 * k + 2] += (int32_t)v.z;
+      acc[4 * k + 3] += (int32_t)v.w;
     }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = j < cnt ? p[j] : 0;
   }
+}
+
+// UW consecutive outputs (UW = 4 or 8 bytes-aligned groups) of one row
+template <int UW>
+__device__ __forceinline__ void store_i16(int16_t* p, const int32_t* o) {
+  uint32_t w[UW / 2];
+#pragma unroll
+  for (int k = 0; k < UW / 2; ++k) w[k] = (uint32_t)(uint16_t)o[2 * k] | (uint32_t)(uint16_t)o[2 * k + 1] << 16;
+  if (UW == 8)
+    *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+  else
+    *reinterpret_cast<uint2*>(p) = make_uint2(w[0], w[1]);
+}
+template <int UW>
+__device__ __forceinline__ void store_i8(int8_t* p, const int32_t* o) {
+  uint32_t w[UW / 4];
+#pragma unroll
+  for (int k = 0; k < UW / 4; ++k)
+    w[k] = (uint32_t)(uint8_t)o[4 * k] | (uint32_t)(uint8_t)o[4 * k + 1] << 8 |
+           (uint32_t)(uint8_t)o[4 * k + 2] << 16 | (uint32_t)(uint8_t)o[4 * k + 3] << 24;
+  if (UW == 8)
+    *reinterpret_cast<uint2*>(p) = make_uint2(w[0], w[1]);
+  else
+    *reinterpret_cast<uint32_t*>(p) = w[0];
+}
+template <int UW>
+__device__ __forceinline__ void load_i16(const int16_t* p, int32_t* v) {
+  uint32_t w[UW / 2];
+  if (UW == 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    w[0] = u.x, w[1] = u.y, w[2] = u.z, w[3] = u.w;
+  } else {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    w[0] = u.x, w[1] = u.y;
+  }
+#pragma unroll
+  for (int k = 0; k < UW / 2; ++k) {
+    v[2 * k] = (int16_t)(w[k] & 0xFFFF);
+    v[2 * k + 1] = (int16_t)(w[k] >> 16);
+  }
+}
+
+// Epilogue of UW columns (tile columns c0.., global n0 + c0..) of row r: requant + epilogue
+// + store, or raw int32 partial sums; the fused argmax key of the output linear.  Channel
+// groups never straddle an output segment (segments are 16-channel multiples).
+template <int UW>
+__device__ __forceinline__ void epi_unit(const LinearArgs& a, const int32_t (&acc)[UW], int c0, int n0, int r,
+                                         const int64_t* s_bias, const uint32_t* s_M, const int* s_S,
+                                         const uint16_t* s_sig) {
+  const int nb = n0 + c0;
+  void* dst = a.out;
+  int ld = a.N, col = nb, i8 = a.out_i8;
+  if (a.nseg > 0) {
+    int sgi = 0;
+    while (sgi + 1 < a.nseg && nb >= a.seg_start[sgi + 1]) ++sgi;
+    dst = a.seg_out[sgi];
+    ld = a.seg_start[sgi + 1] - a.seg_start[sgi];
+    col = nb - a.seg_start[sgi];
+    i8 = a.seg_i8[sgi];
+  }
+  if (a.out_i32) {
+    // tensor-parallel partial sums: raw accumulators
+    uint4* p = reinterpret_cast<uint4*>(reinterpret_cast<int32_t*>(dst) + (int64_t)r * ld + col);
+#pragma unroll
+    for (int k = 0; k < UW / 4; ++k)
+      p[k] = make_uint4((uint32_t)acc[4 * k], (uint32_t)acc[4 * k + 1], (uint32_t)acc[4 * k + 2],
+                        (uint32_t)acc[4 * k + 3]);
+    return;
+  }
+  const bool narrow = a.narrow != 0;
+  int32_t o[UW];
+  if (i8) {
+#pragma unroll
+    for (int j = 0; j < UW; ++j) o[j] = requant_sat(acc[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], narrow, -128, 127);
+    store_i8<UW>(reinterpret_cast<int8_t*>(dst) + (int64_t)r * ld + col, o);
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < UW; ++j) o[j] = requant_sat(acc[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], narrow, -32768, 32767);
+  if (a.epi == EPI_RESADD || a.epi == EPI_MUL) {
+    int32_t aux[UW];
+    load_i16<UW>(a.aux + (int64_t)r * a.N + nb, aux);
+    if (a.epi == EPI_RESADD) {
+#pragma unroll
+      for (int j = 0; j < UW; ++j) o[j] = sat16_32(o[j] + aux[j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < UW; ++j) o[j] = sat16_32(rshr_small(o[j] * aux[j], a.aux_shift));
+    }
+  } else if (a.epi == EPI_SILU) {
+    const uint32_t Mi = (uint32_t)a.silu_Mi;
+#pragma unroll
+    for (int j = 0; j < UW; ++j) o[j] = silu_fast(o[j], Mi, a.silu_Si, a.silu_sh, s_sig);
+  }
+  store_i16<UW>(reinterpret_cast<int16_t*>(dst) + (int64_t)r * ld + col, o);
+  if (a.amax_key) {
+    unsigned long long best = 0ull;
+#pragma unroll
+    for (int j = 0; j < UW; ++j) {
+      const int n = nb + j;
+      if (n < a.amax_vocab) {
+        const unsigned long long key =
+            ((unsigned long long)(uint32_t)(o[j] + 32768) << 32) | (0xFFFFFFFFu - (uint32_t)(n + a.amax_base));
+        best = key > best ? key : best;
+      }
+    }
+    if (best) atomicMax(a.amax_key + r, best);
+  }
+}
+
+// Fused gate/up unit: 8 output channels ob.. of row r from gate columns cg.. and up columns cu..
+//   sg = silu16(requant16(acc_g)); f = sat16(rshr(requant16(acc_u) * sg, aux_shift));
+//   fq = sat8(mulshift(f, q_M, q_S))
+__device__ __forceinline__ void epi_gated_unit(const LinearArgs& a, const int32_t (&ag)[8], const int32_t (&au)[8],
+                                               int cg, int cu, int r, int ob, const int64_t* s_bias,
+                                               const uint32_t* s_M, const int* s_S, const uint16_t* s_sig) {
+  const bool narrow = a.narrow != 0;
+  const uint32_t Mi = (uint32_t)a.silu_Mi;
+  int32_t sg[8], f[8], fq[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int32_t tg = requant_sat(ag[j], s_bias[cg + j], s_M[cg + j], s_S[cg + j], narrow, -32768, 32767);
+    const int32_t tu = requant_sat(au[j], s_bias[cu + j], s_M[cu + j], s_S[cu + j], narrow, -32768, 32767);
+    sg[j] = silu_fast(tg, Mi, a.silu_Si, a.silu_sh, s_sig);
+    f[j] = sat16_32(rshr_small(tu * sg[j], a.aux_shift));
+    fq[j] = mulshift_clamp(f[j], (uint32_t)a.q_M, a.q_S, -128, 127);
+  }
+  const int64_t off = (int64_t)r * a.Nout + ob;
+  if (a.g_out) store_i16<8>(a.g_out + off, sg);
+  if (a.f_out) store_i16<8>(a.f_out + off, f);
+  if (a.q_out) store_i8<8>(a.q_out + off, fq);
 }
 
 template <int NT, int S>
@@ -356,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   } else {
     pdl_wait();  // aux rows and the output buffer belong to earlier kernels
-    // ---- epilogue warps 2..9: TMEM lane quarter = warp % 4, chunk parity = (warp - 2) / 4 ----
+    // ---- epilogue warps 2..9: TMEM lane quarter = warp % 4, half = (warp - 2) / 4 ----
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row_in_tile = q * 32 + lane;
@@ -366,18 +479,19 @@ __global__ void __launch_bounds__(kThreads, 2)
       atomicExch(err, 4);
     }
     tc_fence_after();
-    int32_t* part = reinterpret_cast<int32_t*>(ring);  // [BM][NT] partials when ksplit > 1
+    uint4* part4 = reinterpret_cast<uint4*>(ring);  // [NT/4][BM] 4-column groups of the partial tile
     if (ok && ksplit > 1) {
-      // all MMAs are complete, so the ring is free: stage this CTA's partial tile
-      for (int c0 = half * 16; c0 < NT; c0 += 32) {
-        uint32_t v[16];
-        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + c0, v);
+      // all MMAs are complete, so the ring is free: stage this CTA's partial tile, one
+      // 16-byte group per row and 4 columns (rows consecutive: no bank conflicts)
+      for (int u8 = half; u8 < NT / 8; u8 += 2) {
+        uint32_t v[8];
+        tmem_ld8(tmem + ((uint32_t)(q * 32) << 16) + u8 * 8, v);
         if (nkb == 0) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = 0;
+          for (int j = 0; j < 8; ++j) v[j] = 0;
         }
-#pragma unroll
-        for (int j = 0; j < 16; ++j) part[row_in_tile * NT + c0 + j] = (int32_t)v[j];
+        part4[(2 * u8) * BM + row_in_tile] = make_uint4(v[0], v[1], v[2], v[3]);
+        part4[(2 * u8 + 1) * BM + row_in_tile] = make_uint4(v[4], v[5], v[6], v[7]);
       }
     }
   }
@@ -390,141 +504,38 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int half = (warp - 2) >> 2;
     const int row_in_tile = q * 32 + lane;
     const int r = m0 + row_in_tile;
-    const int32_t* part = reinterpret_cast<const int32_t*>(ring);
-    const bool narrow = a.narrow != 0;
-    // 16 accumulators of channel chunk c0..c0+15 for this thread's row (warp-uniform call)
-    auto fetch = [&](int c0, int32_t* acc) {
-      if (ksplit == 1) {
-        uint32_t v[16];
-        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + c0, v);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] = nkb > 0 ? (int32_t)v[j] : 0;
-      } else {
-        // this rank owns chunk c0: sum the partial tiles of every CTA of the cluster
-#pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] = 0;
-        const int32_t* src = part + row_in_tile * NT + c0;
-        for (uint32_t p = 0; p < (uint32_t)ksplit; ++p) {
-          uint4 v[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) v[k] = dsmem_ld4(src + 4 * k, p);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            acc[4 * k] += (int32_t)v[k].x;
-            acc[4 * k + 1] += (int32_t)v[k].y;
-            acc[4 * k + 2] += (int32_t)v[k].z;
-            acc[4 * k + 3] += (int32_t)v[k].w;
-          }
-        }
-      }
-    };
+    const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+    const uint4* part4 = reinterpret_cast<const uint4*>(ring);
+    // work units of UW columns go round-robin over the cluster's CTAs, then the two warp
+    // halves: unit u -> CTA u % ksplit, half (u / ksplit) % 2
+    const int first = (int)crank + ksplit * half, stride = 2 * ksplit;
     if (a.gated) {
-      // chunk pairs (gate, up) -> 16 output channels; pairs alternate between the two warps
+      // unit v = 8 outputs: gate columns 32 (v/2) + 8 (v%2) .. +7, up columns 16 further
 #pragma unroll 1
-      for (int ci = 0; ci < NT / 32; ++ci) {
-        if (ci % ksplit != (int)crank || (ci / ksplit) % 2 != half) continue;
-        const int c0 = ci * 32;
-        int32_t ag[16], au[16];
-        fetch(c0, ag);
-        fetch(c0 + 16, au);
+      for (int v = first; v < NT / 16; v += stride) {
+        const int cg = 32 * (v >> 1) + 8 * (v & 1), cu = cg + 16;
+        int32_t ag[8], au[8];
+        epi_fetch<8>(ag, trow, part4, row_in_tile, cg, ksplit, nkb);
+        epi_fetch<8>(au, trow, part4, row_in_tile, cu, ksplit, nkb);
         if (r >= a.R) continue;
-        const int ob = (n0 + c0) / 2;  // first output channel of this pair
+        const int ob = (n0 + 32 * (v >> 1)) / 2 + 8 * (v & 1);  // first output channel of this unit
         if (ob >= a.Nout) continue;
-        const int cnt = min(16, a.Nout - ob);
-        int32_t sg[16], f[16], fq[16];
-        const uint32_t Mi = (uint32_t)a.silu_Mi;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int32_t tg = requant_sat(ag[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], narrow, -32768, 32767);
-          const int32_t tu =
-              requant_sat(au[j], s_bias[c0 + 16 + j], s_M[c0 + 16 + j], s_S[c0 + 16 + j], narrow, -32768, 32767);
-          sg[j] = silu_fast(tg, Mi, a.silu_Si, a.silu_sh, s_sig);
-          f[j] = sat16_32(rshr_small(tu * sg[j], a.aux_shift));
-          fq[j] = mulshift_clamp(f[j], (uint32_t)a.q_M, a.q_S, -128, 127);
-        }
-        const int64_t off = (int64_t)r * a.Nout + ob;
-        if (a.g_out) store16_i16(a.g_out + off, sg, cnt);
-        if (a.f_out) store16_i16(a.f_out + off, f, cnt);
-        if (a.q_out) store16_i8(a.q_out + off, fq, cnt);
+        epi_gated_unit(a, ag, au, cg, cu, r, ob, s_bias, s_M, s_S, s_sig);
+      }
+    } else if (ksplit > 1) {
+#pragma unroll 1
+      for (int u = first; u < NT / 4; u += stride) {
+        int32_t acc[4];
+        epi_fetch<4>(acc, trow, part4, row_in_tile, 4 * u, ksplit, nkb);
+        if (r < a.R && n0 + 4 * u < a.N) epi_unit<4>(a, acc, 4 * u, n0, r, s_bias, s_M, s_S, s_sig);
       }
     } else {
-      unsigned long long best = 0ull;  // fused argmax key of this thread's row
 #pragma unroll 1
-      for (int ci = 0; ci < NT / 16; ++ci) {
-        if (ci % ksplit != (int)crank || (ci / ksplit) % 2 != half) continue;
-        const int c0 = ci * 16;
-        int32_t acc[16];
-        fetch(c0, acc);
-        if (r >= a.R) continue;
-        const int nb = n0 + c0;
-        if (nb >= a.N) continue;
-        // destination: the single output, or the segment holding this chunk
-        void* dst = a.out;
-        int ld = a.N, col = nb, i8 = a.out_i8, cnt = min(16, a.N - nb);
-        if (a.nseg > 0) {
-          int sgi = 0;
-          while (sgi + 1 < a.nseg && nb >= a.seg_start[sgi + 1]) ++sgi;
-          dst = a.seg_out[sgi];
-          ld = a.seg_start[sgi + 1] - a.seg_start[sgi];
-          col = nb - a.seg_start[sgi];
-          i8 = a.seg_i8[sgi];
-          cnt = min(16, a.seg_start[sgi + 1] - nb);
-        }
-        if (a.out_i32) {
-          // tensor-parallel partial sums: raw accumulators, 64 bytes per row chunk
-          int32_t* p = reinterpret_cast<int32_t*>(dst) + (int64_t)r * ld + col;
-          if (cnt == 16) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-              reinterpret_cast<uint4*>(p)[k] = make_uint4((uint32_t)acc[4 * k], (uint32_t)acc[4 * k + 1],
-                                                          (uint32_t)acc[4 * k + 2], (uint32_t)acc[4 * k + 3]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              if (j < cnt) p[j] = acc[j];
-          }
-          continue;
-        }
-        int32_t o[16];
-        if (i8) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            o[j] = requant_sat(acc[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], narrow, -128, 127);
-          store16_i8(reinterpret_cast<int8_t*>(dst) + (int64_t)r * ld + col, o, cnt);
-          continue;
-        }
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          o[j] = requant_sat(acc[j], s_bias[c0 + j], s_M[c0 + j], s_S[c0 + j], narrow, -32768, 32767);
-        if (a.epi == EPI_RESADD || a.epi == EPI_MUL) {
-          int32_t aux[16];
-          load16_i16(a.aux + (int64_t)r * a.N + nb, aux, cnt);
-          if (a.epi == EPI_RESADD) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) o[j] = sat16_32(o[j] + aux[j]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) o[j] = sat16_32(rshr_small(o[j] * aux[j], a.aux_shift));
-          }
-        } else if (a.epi == EPI_SILU) {
-          const uint32_t Mi = (uint32_t)a.silu_Mi;
-#pragma unroll
-          for (int j = 0; j < 16; ++j) o[j] = silu_fast(o[j], Mi, a.silu_Si, a.silu_sh, s_sig);
-        }
-        store16_i16(reinterpret_cast<int16_t*>(dst) + (int64_t)r * ld + col, o, cnt);
-        if (a.amax_key) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int n = nb + j;
-            if (j < cnt && n < a.amax_vocab) {
-              const unsigned long long key =
-                  ((unsigned long long)(uint32_t)(o[j] + 32768) << 32) | (0xFFFFFFFFu - (uint32_t)(n + a.amax_base));
-              best = key > best ? key : best;
-            }
-          }
-        }
+      for (int u = first; u < NT / 8; u += stride) {
+        int32_t acc[8];
+        epi_fetch<8>(acc, trow, part4, row_in_tile, 8 * u, ksplit, nkb);
+        if (r < a.R && n0 + 8 * u < a.N) epi_unit<8>(a, acc, 8 * u, n0, r, s_bias, s_M, s_S, s_sig);
       }
-      if (a.amax_key && best && r < a.R) atomicMax(a.amax_key + r, best);
     }
   }
   if (ksplit > 1) cluster_sync();  // peers keep their shared memory until rank 0 has read it
