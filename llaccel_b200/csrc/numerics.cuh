@@ -53,6 +53,25 @@ __device__ __forceinline__ uint32_t isqrt48(uint64_t t) {
 // unsigned division with b == 0 read as 1, truncated to u32 (numerics.h:36)
 __device__ __forceinline__ uint32_t udiv(uint64_t a, uint64_t b) { return (uint32_t)(a / (b ? b : 1)); }
 
+// isqrt48 through the hardware double square root, then corrected to the exact floor with
+// integer products: for t < 2^48 the double result is within one unit of floor(sqrt(t)),
+// and each correction step runs at most once.
+__device__ __forceinline__ uint32_t isqrt48_fast(uint64_t t) {
+  uint64_t r = (uint64_t)sqrt((double)t);
+  if (r * r > t) --r;
+  if ((r + 1) * (r + 1) <= t) ++r;
+  return (uint32_t)r;
+}
+
+// floor(a / b) for a < 2^53, 1 <= b < 2^32 through a double divide, corrected to the exact
+// quotient with integer products (the double quotient is within one unit of it).
+__device__ __forceinline__ uint64_t udiv_fast(uint64_t a, uint32_t b) {
+  uint64_t q = (uint64_t)((double)a / (double)b);
+  if (q * b > a) --q;
+  if ((q + 1) * b <= a) ++q;
+  return q;
+}
+
 // LUT SiLU with linear interpolation (numerics.h:45-51; NUMERICS.md:127-139)
 __device__ __forceinline__ int64_t silu16(int64_t x, int64_t Mi, int Si, int sh_out, const uint16_t* __restrict__ sig) {
   const int64_t u = sat16(mulshift(x, Mi, Si));

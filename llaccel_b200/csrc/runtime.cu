@@ -160,6 +160,7 @@ struct llx_model {
   int input_act = 0, output_act = -1;
   int tail_start = 0;
   std::vector<int> tail_inputs;
+  std::vector<int> act_uses;  // steps that read each activation (fused groups count once)
   int64_t embed_off = -1, cos_off = -1, sin_off = -1;
   int embed_rows = 0;
   std::vector<uint8_t> blob_host_check;  // unused after upload
@@ -696,6 +697,10 @@ static void build_plan(llx_model* m, const json::Value& g, std::vector<uint8_t>&
   auto it = m->act_id.find(out_name);
   require(it != m->act_id.end(), LLX_ERR_INVALID, "qgraph output '" + out_name + "' is never produced");
   m->output_act = it->second;
+  m->act_uses.assign(m->acts.size(), 0);
+  for (const Step& x : m->steps)
+    for (int a : step_ins(x)) m->act_uses[a]++;
+  m->act_uses[m->output_act]++;
   require(m->acts[m->output_act].elem == 2 && m->acts[m->output_act].cols == m->vocab_padded, LLX_ERR_INVALID,
           "output must be i16 [M][vocab_padded]");
   // row-independent tail: everything after the last attention / KV write
@@ -972,6 +977,8 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
   llx_model* m = s->m;
   cudaStream_t st = s->st;
   auto P = [&](int a) { return a < 0 ? nullptr : bd.p[a]; };
+  // an output that no later step reads (and no dump keeps) is not stored
+  auto Pused = [&](int a) { return (a < 0 || (!s->keep && m->act_uses[a] == 0)) ? nullptr : bd.p[a]; };
   {
     cudaError_t e = cudaSuccess;
     switch (x.kind) {
@@ -1070,7 +1077,8 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
       }
       case SK::Rope: {
         int8_t* kc = x.write_k ? s->kv_layer.at(x.layer).first : nullptr;
-        e = launch_rope((const int16_t*)P(x.in), (int16_t*)P(x.out), (int8_t*)P(x.out2), x.Mq, x.Sq, kc, R, M, x.H,
+        e = launch_rope((const int16_t*)P(x.in), (int16_t*)(x.out2 >= 0 ? Pused(x.out) : P(x.out)), (int8_t*)P(x.out2),
+                        x.Mq, x.Sq, kc, R, M, x.H,
                         x.D, (const int16_t*)dptr(m, m->cos_off), (const int16_t*)dptr(m, m->sin_off), s->d_pos,
                         m->max_seq, st);
         break;
@@ -1139,8 +1147,8 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
           a.silu_Si = g.silu_Si;
           a.silu_sh = g.silu_sh;
           a.aux_shift = u.aux_shift;
-          a.g_out = (int16_t*)P(g.out);
-          a.f_out = (int16_t*)P(u.out);
+          a.g_out = (int16_t*)Pused(g.out);
+          a.f_out = (int16_t*)(x.parts.size() > 2 ? Pused(u.out) : P(u.out));
           if (x.parts.size() > 2) {
             a.q_out = (int8_t*)P(x.parts[2].out);
             a.q_M = x.parts[2].Mq;
@@ -1163,8 +1171,8 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
         const Step& k = x.parts[1];
         const Step& v = x.parts[2];
         auto kv = s->kv_layer.at(k.layer);
-        RopeJob jq{(const int16_t*)P(q.in), (int16_t*)P(q.out), (int8_t*)P(q.out2), q.Mq, q.Sq, nullptr, q.H};
-        RopeJob jk{(const int16_t*)P(k.in), (int16_t*)P(k.out), (int8_t*)P(k.out2), k.Mq, k.Sq, kv.first, k.H};
+        RopeJob jq{(const int16_t*)P(q.in), (int16_t*)Pused(q.out), (int8_t*)P(q.out2), q.Mq, q.Sq, nullptr, q.H};
+        RopeJob jk{(const int16_t*)P(k.in), (int16_t*)Pused(k.out), (int8_t*)P(k.out2), k.Mq, k.Sq, kv.first, k.H};
         e = launch_rope_group(jq, jk, (const int8_t*)P(v.in2), s->kv_layer.at(v.layer).second, v.Hkv, R, M, q.D,
                               (const int16_t*)dptr(m, m->cos_off), (const int16_t*)dptr(m, m->sin_off), s->d_pos,
                               m->max_seq, st);
