@@ -473,11 +473,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row_in_tile = q * 32 + lane;
-    const bool ok = mbar_wait(&acc_bar, 0, &abort_flag);
-    if (!ok) {
+    // one thread polls the accumulator barrier; the eight epilogue warps then meet at named
+    // barrier 1, which issues nothing while the main loop runs
+    if (warp == 2 && lane == 0 && !mbar_wait(&acc_bar, 0, &abort_flag)) {
       abort_flag = 1;
       atomicExch(err, 4);
     }
+    asm volatile("bar.sync 1, %0;" ::"n"(kThreads - 64) : "memory");
+    const bool ok = abort_flag == 0;
     tc_fence_after();
     uint4* part4 = reinterpret_cast<uint4*>(ring);  // [NT/4][BM] 4-column groups of the partial tile
     if (ok && ksplit > 1) {

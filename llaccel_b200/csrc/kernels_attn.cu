@@ -245,7 +245,6 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
     const uint16_t* __restrict__ luts, int32_t* err, int C) {
   constexpr int D = LPK * 16;
   constexpr int TK = dec_tile_keys(D);
-  constexpr int D4 = D / 4;  // 4-channel value units per head
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ uint16_t s_expi[16], s_expf[256];
   __shared__ __align__(8) uint64_t full_bar[kRing];
@@ -299,8 +298,10 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   const int8_t* qrow = q + ((int64_t)b * H + (int64_t)kvh * rep_all + hg0) * D;
   for (int i = threadIdx.x; i < rep * D / 16; i += blockDim.x)
     reinterpret_cast<uint4*>(q_s)[i] = reinterpret_cast<const uint4*>(qrow)[i];
+  // one thread polls the stage's barrier; the others wait at the CTA barrier, which issues
+  // nothing (a CTA-wide poll would take issue slots from the CTAs sharing the SM)
   auto wait_stage = [&](int i) {
-    if (s_abort == 0 && !att_mbar_wait(&full_bar[i % kRing], (uint32_t)((i / kRing) & 1))) {
+    if (threadIdx.x == 0 && s_abort == 0 && !att_mbar_wait(&full_bar[i % kRing], (uint32_t)((i / kRing) & 1))) {
       s_abort = 1;
       if (err) atomicExch(err, 5);
     }
@@ -436,6 +437,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   }
   __syncthreads();
   // ---- V slice: unit u = (head j, 4 channels) accumulates over the slice's keys in pairs ----
+  constexpr int D4 = D / 4;
   int32_t acc[2][4];
 #pragma unroll
   for (int x = 0; x < 2; ++x)
