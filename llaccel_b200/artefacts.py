@@ -567,13 +567,98 @@ def init_weights(cfg: ArchConfig, seed: int, device: str = "cpu") -> dict:
     return W
 
 
-def calibrate(cfg: ArchConfig, W: dict, sequences: list[list[int]], device: str = "cpu") -> dict:
-    """Abs-max of every named activation and RMS minimum of every RMSNorm input over
-    `sequences`, from a float32 forward pass of the architecture (calibrate.py:95-133)."""
+def float_forward(cfg: ArchConfig, W: dict, ids: list[int], device: str = "cpu", rec=None, rec_rms=None):
+    """Float32 forward of the architecture over one token sequence (causal, one pass);
+    returns logits [T][vocab].  `rec(name, t)` / `rec_rms(name, t, width)` observe the named
+    activations (the calibration hooks of calibrate.py:95-133)."""
     import torch
     import torch.nn.functional as F
 
+    rec = rec or (lambda name, t: None)
+    rec_rms = rec_rms or (lambda name, t, width: None)
     H, Hkv, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+
+    def norm(x, w):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.rms_eps) * w
+
+    inv = cfg.rope_base ** (-torch.arange(0, D, 2, dtype=torch.float32, device=device) / D)
+    with torch.no_grad():
+        T = len(ids)
+        tok = torch.tensor(ids, dtype=torch.long, device=device)
+        ang = torch.outer(torch.arange(T, dtype=torch.float32, device=device), inv)
+        ang = torch.cat((ang, ang), dim=-1)
+        cos, sin = ang.cos(), ang.sin()
+
+        def rot(x):  # x [H, T, D]
+            half = D // 2
+            return x * cos + torch.cat((-x[..., half:], x[..., :half]), -1) * sin
+
+        x = W["embed"][tok]
+        rec("input", x)
+        resid = "input"
+        for i in range(cfg.n_layers):
+            p = f"l{i}"
+            rec_rms(resid, x, cfg.dim)
+            h = norm(x, W[f"{p}_attn_norm"])
+            rec(f"{p}.h", h)
+            q = h @ W[f"{p}_wq"].T
+            k = h @ W[f"{p}_wk"].T
+            v = h @ W[f"{p}_wv"].T
+            if cfg.qkv_bias:
+                q, k, v = q + W[f"{p}_bq"], k + W[f"{p}_bk"], v + W[f"{p}_bv"]
+            rec(f"{p}.q", q)
+            rec(f"{p}.k", k)
+            rec(f"{p}.v", v)
+            q = q.view(T, H, D)
+            k = k.view(T, Hkv, D)
+            if cfg.qk_norm:
+                rec_rms(f"{p}.q", q, D)
+                rec_rms(f"{p}.k", k, D)
+                q = norm(q, W[f"{p}_q_norm"])
+                k = norm(k, W[f"{p}_k_norm"])
+                rec(f"{p}.qn", q)
+                rec(f"{p}.kn", k)
+            qr = rot(q.transpose(0, 1))
+            kr = rot(k.transpose(0, 1))
+            rec(f"{p}.qr", qr)
+            rec(f"{p}.kr", kr)
+            vv = v.view(T, Hkv, D).transpose(0, 1)
+            rep = H // Hkv
+            a = F.scaled_dot_product_attention(qr[None], kr.repeat_interleave(rep, 0)[None],
+                                               vv.repeat_interleave(rep, 0)[None], is_causal=True)[0]
+            a = a.transpose(0, 1).reshape(T, H * D)
+            rec(f"{p}.a", a)
+            o = a @ W[f"{p}_wo"].T
+            rec(f"{p}.o", o)
+            x1 = x + o
+            rec(f"{p}.x1", x1)
+            rec_rms(f"{p}.x1", x1, cfg.dim)
+            h2 = norm(x1, W[f"{p}_ffn_norm"])
+            rec(f"{p}.h2", h2)
+            g = h2 @ W[f"{p}_wg"].T
+            u = h2 @ W[f"{p}_wu"].T
+            rec(f"{p}.g", g)
+            rec(f"{p}.u", u)
+            sg = F.silu(g)
+            rec(f"{p}.sg", sg)
+            f = sg * u
+            rec(f"{p}.f", f)
+            d = f @ W[f"{p}_wd"].T
+            rec(f"{p}.d", d)
+            x = x1 + d
+            rec(f"{p}.x2", x)
+            resid = f"{p}.x2"
+        rec_rms(resid, x, cfg.dim)
+        hn = norm(x, W["norm"])
+        rec("hn", hn)
+        logits = hn @ W["lm_head"].T
+        rec("logits", logits)
+        return logits
+
+
+def calibrate(cfg: ArchConfig, W: dict, sequences: list[list[int]], device: str = "cpu") -> dict:
+    """Abs-max of every named activation and RMS minimum of every RMSNorm input over
+    `sequences`, from a float32 forward pass of the architecture (calibrate.py:95-133)."""
     absmax: dict[str, float] = {}
     rms_min: dict[str, float] = {}
 
@@ -587,81 +672,8 @@ def calibrate(cfg: ArchConfig, W: dict, sequences: list[list[int]], device: str 
         r = float(t.double().reshape(-1, width).square().mean(-1).sqrt().min())
         rms_min[name] = min(rms_min.get(name, float("inf")), r)
 
-    def norm(x, w):
-        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.rms_eps) * w
-
-    inv = cfg.rope_base ** (-torch.arange(0, D, 2, dtype=torch.float32, device=device) / D)
-    with torch.no_grad():
-        for ids in sequences:
-            T = len(ids)
-            tok = torch.tensor(ids, dtype=torch.long, device=device)
-            ang = torch.outer(torch.arange(T, dtype=torch.float32, device=device), inv)
-            ang = torch.cat((ang, ang), dim=-1)
-            cos, sin = ang.cos(), ang.sin()
-
-            def rot(x):  # x [H, T, D]
-                half = D // 2
-                return x * cos + torch.cat((-x[..., half:], x[..., :half]), -1) * sin
-
-            x = W["embed"][tok]
-            rec("input", x)
-            resid = "input"
-            for i in range(cfg.n_layers):
-                p = f"l{i}"
-                rec_rms(resid, x, cfg.dim)
-                h = norm(x, W[f"{p}_attn_norm"])
-                rec(f"{p}.h", h)
-                q = h @ W[f"{p}_wq"].T
-                k = h @ W[f"{p}_wk"].T
-                v = h @ W[f"{p}_wv"].T
-                if cfg.qkv_bias:
-                    q, k, v = q + W[f"{p}_bq"], k + W[f"{p}_bk"], v + W[f"{p}_bv"]
-                rec(f"{p}.q", q)
-                rec(f"{p}.k", k)
-                rec(f"{p}.v", v)
-                q = q.view(T, H, D)
-                k = k.view(T, Hkv, D)
-                if cfg.qk_norm:
-                    rec_rms(f"{p}.q", q, D)
-                    rec_rms(f"{p}.k", k, D)
-                    q = norm(q, W[f"{p}_q_norm"])
-                    k = norm(k, W[f"{p}_k_norm"])
-                    rec(f"{p}.qn", q)
-                    rec(f"{p}.kn", k)
-                qr = rot(q.transpose(0, 1))
-                kr = rot(k.transpose(0, 1))
-                rec(f"{p}.qr", qr)
-                rec(f"{p}.kr", kr)
-                vv = v.view(T, Hkv, D).transpose(0, 1)
-                rep = H // Hkv
-                a = F.scaled_dot_product_attention(qr[None], kr.repeat_interleave(rep, 0)[None],
-                                                   vv.repeat_interleave(rep, 0)[None], is_causal=True)[0]
-                a = a.transpose(0, 1).reshape(T, H * D)
-                rec(f"{p}.a", a)
-                o = a @ W[f"{p}_wo"].T
-                rec(f"{p}.o", o)
-                x1 = x + o
-                rec(f"{p}.x1", x1)
-                rec_rms(f"{p}.x1", x1, cfg.dim)
-                h2 = norm(x1, W[f"{p}_ffn_norm"])
-                rec(f"{p}.h2", h2)
-                g = h2 @ W[f"{p}_wg"].T
-                u = h2 @ W[f"{p}_wu"].T
-                rec(f"{p}.g", g)
-                rec(f"{p}.u", u)
-                sg = F.silu(g)
-                rec(f"{p}.sg", sg)
-                f = sg * u
-                rec(f"{p}.f", f)
-                d = f @ W[f"{p}_wd"].T
-                rec(f"{p}.d", d)
-                x = x1 + d
-                rec(f"{p}.x2", x)
-                resid = f"{p}.x2"
-            rec_rms(resid, x, cfg.dim)
-            hn = norm(x, W["norm"])
-            rec("hn", hn)
-            rec("logits", hn @ W["lm_head"].T)
+    for ids in sequences:
+        float_forward(cfg, W, ids, device, rec, rec_rms)
     return absmax | {k + ".rms_min": v for k, v in rms_min.items()}
 
 
