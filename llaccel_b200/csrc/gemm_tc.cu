@@ -558,6 +558,203 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
+
+// ---------------------------------------------------------------------------------------
+// Persistent variant for GEMMs with many output tiles (prefill, the vocabulary projection):
+// one CTA per SM walks tiles t = blockIdx.x + j * gridDim.x (channel tiles fastest, so
+// consecutive CTAs share an activation row tile in L2).  The accumulator is double-buffered
+// in TMEM (2 x NT columns): the MMA warp fills buffer j & 1 while the EW epilogue warps drain
+// the other, so the integer epilogue of tile j overlaps the main loop of tile j + 1.
+// Barriers: full/empty per ring stage (TMA <-> MMA), acc_full/acc_empty per buffer
+// (MMA <-> epilogue).  Every wait is bounded; on timeout the CTA records an error word and
+// every role stops.  No split-K here (ksplit == 1).
+// ---------------------------------------------------------------------------------------
+template <int NT, int S, int EW>
+__global__ void __launch_bounds__(64 + 32 * EW, 1)
+    k_linear_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+                           LinearArgs a, int32_t* err) {
+  using L = Smem<NT, S>;
+  constexpr int kEpiThreads = 32 * EW;
+  constexpr int kQuads = EW / 4;  // epilogue warps per TMEM lane quarter
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full_bar[S], empty_bar[S], acc_full[2], acc_empty[2];
+  __shared__ uint32_t tmem_base;
+  __shared__ volatile int abort_flag;
+  __shared__ int issued;  // TMA stages issued by the producer (all tiles)
+  __shared__ int64_t s_bias[NT];
+  __shared__ uint32_t s_M[NT];
+  __shared__ int s_S[NT];
+  __shared__ uint16_t s_sig[260];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ntn = (a.N + NT - 1) / NT, ntm = (a.R + BM - 1) / BM;
+  const int tiles = ntn * ntm;
+  const int nkb = (a.K + BK - 1) / BK;
+  const int my_tiles = blockIdx.x < tiles ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 1);
+    }
+    abort_flag = 0;
+    issued = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"(2 * NT));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (a.epi == EPI_SILU || a.gated)
+    for (int i = threadIdx.x; i < 257; i += blockDim.x) s_sig[i] = a.luts[kLutSig + i];
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  pdl_trigger();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer: every k-block of every tile of this CTA through the ring ----
+      int it = 0;
+      bool waited = false;
+      for (int j = 0; j < my_tiles && !abort_flag; ++j) {
+        const int t = blockIdx.x + j * gridDim.x;
+        const int n0 = (t % ntn) * NT, m0 = (t / ntn) * BM;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % S;
+          if (it >= S && !mbar_wait(&empty_bar[s], ((it / S) + 1) & 1, &abort_flag)) {
+            abort_flag = 1;
+            atomicExch(err, 2);
+            break;
+          }
+          uint8_t* sa = ring + s * L::kStage;
+          uint8_t* sb = sa + L::kA;
+          mbar_expect_tx(&full_bar[s], L::kA + L::kB);
+          tma_load_2d(sb, &map_w, &full_bar[s], kb * BK, n0);  // weights: model constants
+          if (!waited) {
+            pdl_wait();  // activations belong to the previous kernel
+            waited = true;
+          }
+          tma_load_2d(sa, &map_a, &full_bar[s], kb * BK, m0);
+          issued = it + 1;
+        }
+      }
+      if (!waited) pdl_wait();
+    } else {
+      pdl_wait();
+    }
+  } else if (warp == 1) {
+    pdl_wait();
+    if (lane == 0) {
+      // ---- MMA issuer: tile j into TMEM buffer j & 1 ----
+      const uint32_t idesc = idesc_i8(NT);
+      int it = 0;
+      for (int j = 0; j < my_tiles && !abort_flag; ++j) {
+        const int b = j & 1, u = j >> 1;
+        if (u > 0 && !mbar_wait(&acc_empty[b], (u - 1) & 1, &abort_flag)) {
+          abort_flag = 1;
+          atomicExch(err, 5);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(b * NT);
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(&full_bar[s], (it / S) & 1, &abort_flag)) {
+            abort_flag = 1;
+            atomicExch(err, 3);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* sa = ring + s * L::kStage;
+          const uint8_t* sb = sa + L::kA;
+          const uint64_t da = smem_desc(sa), db = smem_desc(sb);
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k)
+            mma_i8(acc, da + (uint64_t)(k * 2), db + (uint64_t)(k * 2), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          mma_commit(&empty_bar[s]);
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[b]);  // fires when every MMA of this tile has completed
+      }
+    }
+  } else {
+    pdl_wait();  // aux rows and the output buffer belong to earlier kernels
+    // ---- epilogue warps: TMEM lane quarter = warp % 4, quad = (warp - 2) / 4 ----
+    const int q = warp & 3;
+    const int quad = (warp - 2) >> 2;
+    const int row_in_tile = q * 32 + lane;
+    const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+    for (int j = 0; j < my_tiles; ++j) {
+      const int b = j & 1, u = j >> 1;
+      const int t = blockIdx.x + j * gridDim.x;
+      const int n0 = (t % ntn) * NT, m0 = (t / ntn) * BM;
+      // this tile's requant parameters (the previous tile's epilogue is done with them)
+      for (int i = threadIdx.x - 64; i < NT; i += kEpiThreads) {
+        const int n = n0 + i;
+        s_M[i] = (n < a.N && a.rq) ? (uint32_t)a.rq[2 * n] : 0u;
+        s_S[i] = (n < a.N && a.rq) ? a.rq[2 * n + 1] : 0;
+        s_bias[i] = (n < a.N && a.bias) ? (int64_t)a.bias[n] : 0;
+      }
+      if (warp == 2 && lane == 0 && !abort_flag && !mbar_wait(&acc_full[b], u & 1, &abort_flag)) {
+        abort_flag = 1;
+        atomicExch(err, 4);
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+      if (abort_flag) break;
+      tc_fence_after();
+      const int r = m0 + row_in_tile;
+      const uint32_t tacc = trow + (uint32_t)(b * NT);
+      if (a.gated) {
+#pragma unroll 1
+        for (int v = quad; v < NT / 16; v += kQuads) {
+          const int cg = 32 * (v >> 1) + 8 * (v & 1), cu = cg + 16;
+          int32_t ag[8], au[8];
+          epi_fetch<8>(ag, tacc, nullptr, row_in_tile, cg, 1, nkb);
+          epi_fetch<8>(au, tacc, nullptr, row_in_tile, cu, 1, nkb);
+          if (r >= a.R) continue;
+          const int ob = (n0 + 32 * (v >> 1)) / 2 + 8 * (v & 1);
+          if (ob >= a.Nout) continue;
+          epi_gated_unit(a, ag, au, cg, cu, r, ob, s_bias, s_M, s_S, s_sig);
+        }
+      } else {
+#pragma unroll 1
+        for (int v = quad; v < NT / 8; v += kQuads) {
+          int32_t acc[8];
+          epi_fetch<8>(acc, tacc, nullptr, row_in_tile, 8 * v, 1, nkb);
+          if (r < a.R && n0 + 8 * v < a.N) epi_unit<8>(a, acc, 8 * v, n0, r, s_bias, s_M, s_S, s_sig);
+        }
+      }
+      // every epilogue warp is done reading buffer b (and with s_M etc.): release it
+      tc_fence_before();
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+      if (warp == 2 && lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_empty[b])) : "memory");
+    }
+  }
+  // ---- teardown: drain copies issued but never consumed (abort path), free TMEM ----
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && abort_flag) {
+    for (int i = issued - S > 0 ? issued - S : 0; i < issued; ++i) {
+      for (uint32_t k = 0; k < (1u << 22); ++k)
+        if (mbar_try_wait(&full_bar[i % S], (i / S) & 1)) break;
+    }
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * NT));
+  }
+}
+
 }  // namespace tc
 
 // ---------------------------------------------------------------------------------------
@@ -631,6 +828,37 @@ static cudaError_t launch_tc_t(const CUtensorMap& ma, const CUtensorMap& mw, con
   cfg.attrs = attr;
   cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, tc::k_linear_tc<NT, S>, ma, mw, a, ksplit, err);
+}
+
+template <int NT, int S, int EW>
+static cudaError_t launch_tc_persistent_t(const CUtensorMap& ma, const CUtensorMap& mw, const LinearArgs& a,
+                                          int grid, int32_t* err, cudaStream_t st) {
+  using L = tc::Smem<NT, S>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(tc::k_linear_tc_persistent<NT, S, EW>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const cudaError_t e = launch_k(tc::k_linear_tc_persistent<NT, S, EW>, dim3(grid), dim3(64 + 32 * EW), L::kBytes,
+                                 st, ma, mw, a, err);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+cudaError_t launch_linear_tc_persistent(const CUtensorMap& map_a, const CUtensorMap& map_w, const LinearArgs& a,
+                                        int nt, int sms, int32_t* err, cudaStream_t st) {
+  if (a.R <= 0 || a.N <= 0) return cudaSuccess;
+  const int tiles = (a.N + nt - 1) / nt * ((a.R + tc::BM - 1) / tc::BM);
+  const int grid = tiles < sms ? tiles : sms;
+  switch (nt) {
+    case 128: return launch_tc_persistent_t<128, 6, 16>(map_a, map_w, a, grid, err, st);
+    case 256: return launch_tc_persistent_t<256, 4, 16>(map_a, map_w, a, grid, err, st);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t prepare_linear_tc() { return encode_fn() ? cudaSuccess : cudaErrorNotSupported; }

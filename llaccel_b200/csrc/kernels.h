@@ -129,6 +129,11 @@ cudaError_t make_tmap_i8(CUtensorMap* map, const void* base, int64_t rows, int64
 cudaError_t prepare_linear_tc();
 cudaError_t launch_linear_tc(const CUtensorMap& map_a, const CUtensorMap& map_w, const LinearArgs& a, int nt,
                              int ksplit, int32_t* err, cudaStream_t st);
+// Persistent tensor-core GEMM for many output tiles (no split-K): min(tiles, sms) CTAs walk
+// the tiles with a double-buffered TMEM accumulator, the epilogue of one tile overlapping the
+// main loop of the next.  nt in {128, 256}; map_w with an nt-row box.
+cudaError_t launch_linear_tc_persistent(const CUtensorMap& map_a, const CUtensorMap& map_w, const LinearArgs& a,
+                                        int nt, int sms, int32_t* err, cudaStream_t st);
 
 // ---- attention engine -------------------------------------------------------------------
 struct AttnArgs {

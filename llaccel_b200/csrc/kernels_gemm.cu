@@ -68,15 +68,27 @@ __global__ void __launch_bounds__(256) k_gemv(LinearArgs a) {
 #pragma unroll
   for (int i = 0; i < RB; ++i) acc[i] = 0;
   if (n < a.N) {
+    // four independent 16-byte weight loads in flight per thread before any is consumed:
+    // the weights stream once per launch (HBM-bound), so bytes in flight set the speed
     const uint4* wr = reinterpret_cast<const uint4*>(a.W + (int64_t)n * a.K);
-    for (int k = slot; k < nk; k += 32) {
-      const uint4 wv = __ldg(wr + k);
+    for (int k0 = slot; k0 < nk; k0 += 4 * 32) {
+      uint4 wv[4];
 #pragma unroll
-      for (int i = 0; i < RB; ++i) {
-        const int r = r0 + i;
-        if (r < a.R) {
-          const uint4 xv = __ldg(reinterpret_cast<const uint4*>(a.A + (int64_t)r * a.K) + k);
-          acc[i] = dot16(wv, xv, acc[i]);
+      for (int u = 0; u < 4; ++u) {
+        const int k = k0 + 32 * u;
+        wv[u] = k < nk ? __ldcs(wr + k) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int k = k0 + 32 * u;
+        if (k >= nk) break;
+#pragma unroll
+        for (int i = 0; i < RB; ++i) {
+          const int r = r0 + i;
+          if (r < a.R) {
+            const uint4 xv = __ldg(reinterpret_cast<const uint4*>(a.A + (int64_t)r * a.K) + k);
+            acc[i] = dot16(wv[u], xv, acc[i]);
+          }
         }
       }
     }
@@ -158,7 +170,10 @@ __global__ void __launch_bounds__(256) k_gemm_tiled(LinearArgs a) {
 cudaError_t launch_linear(const LinearArgs& a, int path, cudaStream_t st) {
   if (a.R <= 0 || a.N <= 0) return cudaSuccess;
   if (path == 0) path = a.R <= 16 ? 1 : 2;
-  if (path == 1) {
+  if (path == 1 && a.R == 1) {
+    const dim3 grid((a.N + 7) / 8, 1);
+    { const cudaError_t e_ = launch_k(k_gemv<1>, grid, dim3(256), 0, st, a); if (e_ != cudaSuccess) return e_; }
+  } else if (path == 1) {
     constexpr int RB = 4;
     dim3 grid((a.N + 7) / 8, (a.R + RB - 1) / RB);
     { const cudaError_t e_ = launch_k(k_gemv<RB>, dim3(grid), dim3(256), 0, st, a); if (e_ != cudaSuccess) return e_; }

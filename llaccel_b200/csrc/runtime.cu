@@ -924,6 +924,33 @@ static void pick_tc_tiling(int R, int N, int K, int sms, int* nt, int* ksplit) {
 
 static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, int M);
 
+// One tensor-core GEMM over R rows of activation `in` (N x K weights at a.W).  Many output
+// tiles (at least two per SM: prefill, the vocabulary projection) go to the persistent
+// kernel, whose epilogue overlaps the next tile's main loop; otherwise the per-tile kernel
+// with the widest tile that fills the SMs, or split-K clusters when the tiles are too few.
+static cudaError_t launch_gemm_tc(llx_session* s, const Binding& bd, int in, const LinearArgs& a, bool gated) {
+  llx_model* m = s->m;
+  const int R = a.R, N = a.N, K = a.K;
+  int nt = 16, ks = 1;
+  pick_tc_tiling(R, N, K, m->sms, &nt, &ks);
+  if (gated && nt < 32) {
+    nt = 32;
+    ks = 1;
+  }
+  const int row_tiles = (R + 127) / 128;
+  const CUtensorMap& ma = tmap(s, a.A, (int64_t)bd.rows[in], K, 128);
+  if (ks == 1) {
+    for (int pnt : {256, 128}) {
+      if ((N + pnt - 1) / pnt * row_tiles >= 2 * m->sms) {
+        const CUtensorMap& mw = tmap(s, a.W, N, K, pnt);
+        return launch_linear_tc_persistent(ma, mw, a, pnt, m->sms, s->d_fault, s->st);
+      }
+    }
+  }
+  const CUtensorMap& mw = tmap(s, a.W, N, K, nt);
+  return launch_linear_tc(ma, mw, a, nt, ks, s->d_fault, s->st);
+}
+
 static int enqueue_steps(llx_session* s, const Binding& bd, size_t from, size_t to, int R, int M) {
   int launches = 0;
   for (size_t i = from; i < to; ++i) launches += enqueue_one(s, bd, s->m->steps[i], R, M);
@@ -1018,15 +1045,10 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
           a.amax_vocab = local_vocab(m);
           a.amax_base = m->vocab_base;
         }
-        if (path == 3) {
-          int nt = 16, ks = 1;
-          pick_tc_tiling(R, x.N, x.K, m->sms, &nt, &ks);
-          const CUtensorMap& ma = tmap(s, a.A, (int64_t)bd.rows[x.in], x.K, 128);
-          const CUtensorMap& mw = tmap(s, a.W, x.N, x.K, nt);
-          e = launch_linear_tc(ma, mw, a, nt, ks, s->d_fault, st);
-        } else {
+        if (path == 3)
+          e = launch_gemm_tc(s, bd, x.in, a, false);
+        else
           e = launch_linear(a, path, st);
-        }
         break;
       }
       case SK::LinearPartial: {
@@ -1040,15 +1062,10 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
         a.out_i32 = 1;
         a.luts = m->d_luts;
         const int path = gemm_path_for(m, R);
-        if (path == 3) {
-          int nt = 16, ks = 1;
-          pick_tc_tiling(R, x.N, x.K, m->sms, &nt, &ks);
-          const CUtensorMap& ma = tmap(s, a.A, (int64_t)bd.rows[x.in], x.K, 128);
-          const CUtensorMap& mw = tmap(s, a.W, x.N, x.K, nt);
-          e = launch_linear_tc(ma, mw, a, nt, ks, s->d_fault, st);
-        } else {
+        if (path == 3)
+          e = launch_gemm_tc(s, bd, x.in, a, false);
+        else
           e = launch_linear(a, path, st);
-        }
         break;
       }
       case SK::AllReduce: {
@@ -1155,15 +1172,7 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
             a.q_S = x.parts[2].Sq;
           }
         }
-        int nt = 16, ks = 1;
-        pick_tc_tiling(R, x.N, x.K, m->sms, &nt, &ks);
-        if (x.kind == SK::Gated && nt < 32) {
-          nt = 32;
-          ks = 1;
-        }
-        const CUtensorMap& ma = tmap(s, a.A, (int64_t)bd.rows[x.in], x.K, 128);
-        const CUtensorMap& mw = tmap(s, a.W, x.N, x.K, nt);
-        e = launch_linear_tc(ma, mw, a, nt, ks, s->d_fault, st);
+        e = launch_gemm_tc(s, bd, x.in, a, x.kind == SK::Gated);
         break;
       }
       case SK::RopeGroup: {

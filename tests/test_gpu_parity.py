@@ -226,3 +226,30 @@ def test_host_driven_batch_decode_matches_device_loop(name, B):
             cur[:, 0] = am
         for b in range(B):
             assert [h[b] for h in host] == recs[b]["argmax_per_step"][2 : 2 + n - 1], b
+
+
+@pytest.mark.parametrize("K,N,epi", [(8192, 8192, "resadd"), (1024, 12288, "silu"), (8192, 8192, "mul")])
+def test_persistent_gemm_epilogues_match_oracle(tmp_path, K, N, epi):
+    """Enough output tiles (two per SM) for the persistent double-buffered GEMM, with every
+    epilogue: each CTA drains one TMEM buffer while the next tile accumulates into the other."""
+    R = 1200
+    d = qgraph_synth.build_linear(tmp_path / "lin", K=K, N=N, epi=epi, seed=K + N, max_seq=R)
+    o = O.OracleModel(d)
+    rng = np.random.default_rng(N)
+    rows = rng.integers(-32768, 32768, (R, K))
+    want = o.run_chunk(rows, 0)
+    with CudaModel(d, max_rows=R) as m:
+        np.testing.assert_array_equal(m.run_chunk(rows, 0), want)
+
+
+def test_persistent_gated_prefill_matches_oracle(tmp_path):
+    """A wide FFN prefilled over 20 sequences x 64 rows: the fused gate/up GEMM (silu * up +
+    quant epilogue) runs on the persistent kernel; records equal the oracle's."""
+    d = qgraph_synth.build(tmp_path / "g", dim=256, n_layers=1, H=4, Hkv=2, D=64, ffn=2048, vocab=300, max_seq=96,
+                           seed=5)
+    o = O.OracleModel(d)
+    rng = np.random.default_rng(9)
+    prompts = rng.integers(0, 300, (20, 64)).tolist()
+    want = [o.generate(p, 4) for p in prompts]
+    with CudaModel(d, batch=20, max_rows=64) as m:
+        assert m.generate_batch(prompts, 4, prefill_rows=64) == want
