@@ -250,10 +250,12 @@ __device__ __forceinline__ void load_i16(const int16_t* p, int32_t* v) {
 // Epilogue of UW columns (tile columns c0.., global n0 + c0..) of row r: requant + epilogue
 // + store, or raw int32 partial sums; the fused argmax key of the output linear.  Channel
 // groups never straddle an output segment (segments are 16-channel multiples).
+// `best` collects the row's packed argmax key (output linear only); the caller folds it into
+// amax_key with one atomicMax per thread and row, not one per unit.
 template <int UW>
 __device__ __forceinline__ void epi_unit(const LinearArgs& a, const int32_t (&acc)[UW], int c0, int n0, int r,
                                          const int64_t* s_bias, const uint32_t* s_M, const int* s_S,
-                                         const uint16_t* s_sig) {
+                                         const uint16_t* s_sig, unsigned long long& best) {
   const int nb = n0 + c0;
   void* dst = a.out;
   int ld = a.N, col = nb, i8 = a.out_i8;
@@ -301,7 +303,6 @@ __device__ __forceinline__ void epi_unit(const LinearArgs& a, const int32_t (&ac
   }
   store_i16<UW>(reinterpret_cast<int16_t*>(dst) + (int64_t)r * ld + col, o);
   if (a.amax_key) {
-    unsigned long long best = 0ull;
 #pragma unroll
     for (int j = 0; j < UW; ++j) {
       const int n = nb + j;
@@ -311,7 +312,6 @@ __device__ __forceinline__ void epi_unit(const LinearArgs& a, const int32_t (&ac
         best = key > best ? key : best;
       }
     }
-    if (best) atomicMax(a.amax_key + r, best);
   }
 }
 
@@ -525,20 +525,24 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (ob >= a.Nout) continue;
         epi_gated_unit(a, ag, au, cg, cu, r, ob, s_bias, s_M, s_S, s_sig);
       }
-    } else if (ksplit > 1) {
-#pragma unroll 1
-      for (int u = first; u < NT / 4; u += stride) {
-        int32_t acc[4];
-        epi_fetch<4>(acc, trow, part4, row_in_tile, 4 * u, ksplit, nkb);
-        if (r < a.R && n0 + 4 * u < a.N) epi_unit<4>(a, acc, 4 * u, n0, r, s_bias, s_M, s_S, s_sig);
-      }
     } else {
+      unsigned long long best = 0ull;
+      if (ksplit > 1) {
 #pragma unroll 1
-      for (int u = first; u < NT / 8; u += stride) {
-        int32_t acc[8];
-        epi_fetch<8>(acc, trow, part4, row_in_tile, 8 * u, ksplit, nkb);
-        if (r < a.R && n0 + 8 * u < a.N) epi_unit<8>(a, acc, 8 * u, n0, r, s_bias, s_M, s_S, s_sig);
+        for (int u = first; u < NT / 4; u += stride) {
+          int32_t acc[4];
+          epi_fetch<4>(acc, trow, part4, row_in_tile, 4 * u, ksplit, nkb);
+          if (r < a.R && n0 + 4 * u < a.N) epi_unit<4>(a, acc, 4 * u, n0, r, s_bias, s_M, s_S, s_sig, best);
+        }
+      } else {
+#pragma unroll 1
+        for (int u = first; u < NT / 8; u += stride) {
+          int32_t acc[8];
+          epi_fetch<8>(acc, trow, part4, row_in_tile, 8 * u, ksplit, nkb);
+          if (r < a.R && n0 + 8 * u < a.N) epi_unit<8>(a, acc, 8 * u, n0, r, s_bias, s_M, s_S, s_sig, best);
+        }
       }
+      if (best) atomicMax(a.amax_key + r, best);
     }
   }
   if (ksplit > 1) cluster_sync();  // peers keep their shared memory until rank 0 has read it
@@ -694,6 +698,8 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     const int quad = (warp - 2) >> 2;
     const int row_in_tile = q * 32 + lane;
     const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+    unsigned long long best = 0ull;  // argmax key of row best_r, folded in when the row changes
+    int best_r = -1;
     for (int j = 0; j < my_tiles; ++j) {
       const int b = j & 1, u = j >> 1;
       const int t = blockIdx.x + j * gridDim.x;
@@ -727,11 +733,16 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
           epi_gated_unit(a, ag, au, cg, cu, r, ob, s_bias, s_M, s_S, s_sig);
         }
       } else {
+        if (r != best_r) {
+          if (best) atomicMax(a.amax_key + best_r, best);
+          best = 0ull;
+          best_r = r;
+        }
 #pragma unroll 1
         for (int v = quad; v < NT / 8; v += kQuads) {
           int32_t acc[8];
           epi_fetch<8>(acc, tacc, nullptr, row_in_tile, 8 * v, 1, nkb);
-          if (r < a.R && n0 + 8 * v < a.N) epi_unit<8>(a, acc, 8 * v, n0, r, s_bias, s_M, s_S, s_sig);
+          if (r < a.R && n0 + 8 * v < a.N) epi_unit<8>(a, acc, 8 * v, n0, r, s_bias, s_M, s_S, s_sig, best);
         }
       }
       // every epilogue warp is done reading buffer b (and with s_M etc.): release it
@@ -739,6 +750,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
       asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
       if (warp == 2 && lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_empty[b])) : "memory");
     }
+    if (best) atomicMax(a.amax_key + best_r, best);
   }
   // ---- teardown: drain copies issued but never consumed (abort path), free TMEM ----
   tc_fence_before();
