@@ -278,7 +278,11 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
     else
       s_expf[i - 16] = luts[kLutExpF + i - 16];
   }
-  pdl_wait();  // POS, q and the KV cache come from earlier kernels
+  // POS is written before the launch's first kernel (host copy, or the previous replay's
+  // finalize step), so it is stable here.  The cached keys and values below position pos
+  // were written by earlier launches: their first tiles are requested before the grid
+  // dependency wait, overlapping the previous kernel.  The tile holding position pos, which
+  // this launch's RoPE step writes, is requested after the wait.
   const int T = *d_pos + 1;
   const int chunk = (T + C - 1) / C;
   const int k0 = min(T, (int)crank * chunk), k1 = min(T, k0 + chunk);
@@ -292,9 +296,18 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
     att_bulk_load(ring + (size_t)(i % kRing) * TK * D, (kv ? vbase : kbase) + (int64_t)t0 * D, (uint32_t)(nk * D),
                   &full_bar[i % kRing]);
   };
+  auto fresh = [&](int i) {  // tile i holds position pos = T - 1
+    const int ti = i >= ntile ? i - ntile : i;
+    return ti == ntile - 1 && k1 == T;
+  };
   __syncthreads();
   if (threadIdx.x == 0)
-    for (int i = 0; i < min(kRing, 2 * ntile); ++i) issue(i);
+    for (int i = 0; i < min(kRing, 2 * ntile); ++i)
+      if (!fresh(i)) issue(i);
+  pdl_wait();  // q and the newest K/V row come from earlier kernels
+  if (threadIdx.x == 0)
+    for (int i = 0; i < min(kRing, 2 * ntile); ++i)
+      if (fresh(i)) issue(i);
   const int8_t* qrow = q + ((int64_t)b * H + (int64_t)kvh * rep_all + hg0) * D;
   for (int i = threadIdx.x; i < rep * D / 16; i += blockDim.x)
     reinterpret_cast<uint4*>(q_s)[i] = reinterpret_cast<const uint4*>(qrow)[i];
