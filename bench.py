@@ -327,6 +327,8 @@ def _by_kind(prof: list[dict]) -> dict:
     """Per-step kernel time summed by kind (linear steps split by output role)."""
     out: dict[str, list] = {}
     for p in prof:
+        if p["ms"] <= 0:
+            continue
         kind, _, name = p["label"].partition(":")
         if kind == "linear":
             role = name.split(".")[-1] if "." in name else name
@@ -353,6 +355,8 @@ def _by_kernel(prof: list[dict], rows: int) -> dict:
     algorithmic bytes.  Below 16 rows the linears run on the CUDA-core GEMV kernel."""
     out: dict[str, dict] = {}
     for p in prof:
+        if p["ms"] <= 0:  # a step folded into its neighbour launches nothing
+            continue
         kind = p["label"].partition(":")[0]
         k = _KERNEL_OF.get(kind, kind)
         if k == "k_linear_tc" and rows < 16:

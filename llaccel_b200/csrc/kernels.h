@@ -149,6 +149,19 @@ struct AttnArgs {
   int prob_bits;
   const uint16_t* luts;  // device tables (exp LUTs)
   int32_t* err;          // device error word (a bounded wait timed out)
+  // Decode (M = 1) with the layer's RoPE group folded in (rq16 non-null): rq16 / rk16 are
+  // the unrotated i16 rows [B][H*D] / [B][Hkv*D], rv8 the quantized values [B][Hkv*D].  The
+  // kernel rotates and quantizes q and the newest key, writes the newest K and V rows to the
+  // caches and uses them directly (RoPE: numerics.h:75-84).
+  const int16_t* rq16;
+  const int16_t* rk16;
+  const int8_t* rv8;
+  int8_t* kc_out;  // the caches kc / vc, written at position pos
+  int8_t* vc_out;
+  const int16_t* cos_tab;
+  const int16_t* sin_tab;
+  int64_t q_M, k_M;
+  int q_S, k_S;
 };
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st);
 // opt the attention kernel into `smem` bytes of dynamic shared memory (once per device, before capture)

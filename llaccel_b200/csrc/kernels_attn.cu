@@ -242,7 +242,7 @@ template <int LPK, int RB>
 __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
     const int8_t* __restrict__ q, const int8_t* __restrict__ kc, const int8_t* __restrict__ vc, int8_t* __restrict__ out,
     int H, int Hkv, int max_seq, const int* __restrict__ d_pos, int64_t Ms, int Ss, int64_t Mo, int So, int prob_bits,
-    const uint16_t* __restrict__ luts, int32_t* err, int C) {
+    const uint16_t* __restrict__ luts, int32_t* err, int C, const AttnArgs rope) {
   constexpr int D = LPK * 16;
   constexpr int TK = dec_tile_keys(D);
   extern __shared__ __align__(128) unsigned char smem[];
@@ -251,6 +251,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   __shared__ int s_abort;
   __shared__ int32_t s_gmax[RB];
   __shared__ uint32_t s_inv[RB];
+  __shared__ __align__(16) int8_t s_knew[D], s_vnew[D];  // the newest key / value row (folded RoPE)
   const int rep_all = H / Hkv;
   const int hg0 = blockIdx.z * RB;
   const int rep = min(RB, rep_all - hg0);
@@ -300,17 +301,62 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
     const int ti = i >= ntile ? i - ntile : i;
     return ti == ntile - 1 && k1 == T;
   };
+  // with the RoPE group folded in, the tile holding pos is patched after it lands
+  const bool folded = rope.rq16 != nullptr;
+  const bool owner = folded && nkeys > 0 && k1 == T;  // this slice holds position pos
   __syncthreads();
   if (threadIdx.x == 0)
     for (int i = 0; i < min(kRing, 2 * ntile); ++i)
-      if (!fresh(i)) issue(i);
+      if (folded || !fresh(i)) issue(i);
   pdl_wait();  // q and the newest K/V row come from earlier kernels
-  if (threadIdx.x == 0)
+  if (threadIdx.x == 0 && !folded)
     for (int i = 0; i < min(kRing, 2 * ntile); ++i)
       if (fresh(i)) issue(i);
-  const int8_t* qrow = q + ((int64_t)b * H + (int64_t)kvh * rep_all + hg0) * D;
-  for (int i = threadIdx.x; i < rep * D / 16; i += blockDim.x)
-    reinterpret_cast<uint4*>(q_s)[i] = reinterpret_cast<const uint4*>(qrow)[i];
+  if (folded) {
+    // rotate + quantize this CTA's query heads; the slice owner also rotates the newest key
+    // and writes the newest K / V rows to the caches (one head group writes them)
+    const int half = D / 2, pos = T - 1;
+    const int16_t* ct = rope.cos_tab + (int64_t)pos * half;
+    const int16_t* stb = rope.sin_tab + (int64_t)pos * half;
+    for (int idx = threadIdx.x; idx < (rep + 1) * half; idx += blockDim.x) {
+      const int r = idx / half, i = idx % half;
+      if (r == rep && !owner) break;
+      const int16_t* x = r < rep ? rope.rq16 + ((int64_t)b * H + (int64_t)kvh * rep_all + hg0 + r) * D
+                                 : rope.rk16 + ((int64_t)b * Hkv + kvh) * D;
+      const int64_t x1 = x[i], x2 = x[i + half], c = ct[i], sn = stb[i];
+      const int64_t ya = sat16(rshr(x1 * c - x2 * sn, 14));
+      const int64_t yb = sat16(rshr(x2 * c + x1 * sn, 14));
+      const int64_t M = r < rep ? rope.q_M : rope.k_M;
+      const int S = r < rep ? rope.q_S : rope.k_S;
+      int8_t* dst = r < rep ? q_s + r * D : s_knew;
+      dst[i] = (int8_t)sat8(mulshift(ya, M, S));
+      dst[i + half] = (int8_t)sat8(mulshift(yb, M, S));
+    }
+    if (owner)
+      for (int i = threadIdx.x; i < D; i += blockDim.x) s_vnew[i] = rope.rv8[((int64_t)b * Hkv + kvh) * D + i];
+    __syncthreads();
+    if (owner && blockIdx.z == 0)
+      for (int i = threadIdx.x; i < D; i += blockDim.x) {
+        const int64_t o = (((int64_t)b * Hkv + kvh) * max_seq + pos) * D + i;
+        rope.kc_out[o] = s_knew[i];
+        rope.vc_out[o] = s_vnew[i];
+      }
+  } else {
+    const int8_t* qrow = q + ((int64_t)b * H + (int64_t)kvh * rep_all + hg0) * D;
+    for (int i = threadIdx.x; i < rep * D / 16; i += blockDim.x)
+      reinterpret_cast<uint4*>(q_s)[i] = reinterpret_cast<const uint4*>(qrow)[i];
+  }
+  // the newest row of a landed tile is stale cache content under the folded RoPE: replace it
+  auto patch = [&](int i) {
+    if (!owner || !fresh(i)) return;
+    int8_t* tile = ring + (size_t)(i % kRing) * TK * D;
+    const int ti = i >= ntile ? i - ntile : i;
+    int8_t* row = tile + (size_t)(T - 1 - (k0 + ti * TK)) * D;
+    const int8_t* src = i >= ntile ? s_vnew : s_knew;
+    for (int c = threadIdx.x; c < D / 16; c += blockDim.x)
+      reinterpret_cast<uint4*>(row)[c] = reinterpret_cast<const uint4*>(src)[c];
+    __syncthreads();
+  };
   // one thread polls the stage's barrier; the others wait at the CTA barrier, which issues
   // nothing (a CTA-wide poll would take issue slots from the CTAs sharing the SM)
   auto wait_stage = [&](int i) {
@@ -328,6 +374,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   for (int j = 0; j < RB; ++j) mxl[j] = INT_MIN;
   for (int i = 0; i < ntile; ++i) {
     if (!wait_stage(i)) break;
+    patch(i);
     const int8_t* tile = ring + (size_t)(i % kRing) * TK * D;
     const int lt0 = i * TK, nk = min(TK, nkeys - lt0);
     for (int l = threadIdx.x; l < nk; l += kDecThreads) {
@@ -459,6 +506,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   const int units = rep * D4;
   for (int i = ntile; i < 2 * ntile; ++i) {
     if (!wait_stage(i)) break;
+    patch(i);
     const int8_t* tile = ring + (size_t)(i % kRing) * TK * D;
     const int lt0 = (i - ntile) * TK, nk = min(TK, nkeys - lt0);
 #pragma unroll
@@ -566,7 +614,7 @@ static cudaError_t launch_dec_rb(const AttnArgs& a, cudaStream_t st) {
   const size_t smem = dec_smem_bytes(RB, LPK * 16, a.max_seq, C);
   const cudaError_t e = launch_kc(k_attention_decode<LPK, RB>, dim3(a.B * C, a.Hkv, groups), dim3(kDecThreads), smem,
                                   st, dim3(C, 1, 1), a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos, a.Ms, a.Ss,
-                                  a.Mo, a.So, a.prob_bits, a.luts, a.err, C);
+                                  a.Mo, a.So, a.prob_bits, a.luts, a.err, C, a);
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 

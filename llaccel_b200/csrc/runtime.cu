@@ -104,6 +104,10 @@ struct Step {
   // apply, e.g. on the CUDA-core GEMM path) and the concatenated / interleaved weights
   std::vector<Step> parts;
   int nseg = 0;
+  // decode (M = 1): a RoPE group folded into the following attention step (attention ->
+  // index of that RoPE group step; the RoPE group -> folded)
+  int rope_step = -1;
+  bool folded = false;
   int seg_start[5] = {0, 0, 0, 0, 0};
 };
 
@@ -701,6 +705,24 @@ static void build_plan(llx_model* m, const json::Value& g, std::vector<uint8_t>&
   for (const Step& x : m->steps)
     for (int a : step_ins(x)) m->act_uses[a]++;
   m->act_uses[m->output_act]++;
+  // a RoPE group directly before the attention it feeds folds into the decode attention when
+  // nothing else reads its rotated rows (the quantized q goes only to the attention)
+  for (size_t i = 1; i < m->steps.size(); ++i) {
+    Step& at = m->steps[i];
+    Step& rg = m->steps[i - 1];
+    if (at.kind != SK::Attention || rg.kind != SK::RopeGroup || rg.parts.size() != 3) continue;
+    const Step& q = rg.parts[0];
+    const Step& k = rg.parts[1];
+    const Step& v = rg.parts[2];
+    const bool ok = q.out2 == at.in && m->act_uses[at.in] == 1 && m->act_uses[q.out] == 0 &&
+                    m->act_uses[k.out] == 0 && (k.out2 < 0 || m->act_uses[k.out2] == 0) && k.layer == at.layer &&
+                    v.layer == at.layer && q.D == at.D && k.H == at.Hkv && q.H == at.H && v.in2 >= 0 &&
+                    m->acts[v.in2].elem == 1 && (at.D == 16 || at.D == 32 || at.D == 64 || at.D == 128 || at.D == 256);
+    if (ok) {
+      at.rope_step = (int)i - 1;
+      rg.folded = true;
+    }
+  }
   require(m->acts[m->output_act].elem == 2 && m->acts[m->output_act].cols == m->vocab_padded, LLX_ERR_INVALID,
           "output must be i16 [M][vocab_padded]");
   // row-independent tail: everything after the last attention / KV write
@@ -1127,6 +1149,23 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
         a.prob_bits = x.prob_bits;
         a.luts = m->d_luts;
         a.err = s->d_fault;
+        if (M == 1 && x.rope_step >= 0 && !s->keep) {
+          const Step& rg = m->steps[x.rope_step];
+          const Step& q = rg.parts[0];
+          const Step& k = rg.parts[1];
+          const Step& v = rg.parts[2];
+          a.rq16 = (const int16_t*)P(q.in);
+          a.rk16 = (const int16_t*)P(k.in);
+          a.rv8 = (const int8_t*)P(v.in2);
+          a.kc_out = kv.first;
+          a.vc_out = kv.second;
+          a.cos_tab = (const int16_t*)dptr(m, m->cos_off);
+          a.sin_tab = (const int16_t*)dptr(m, m->sin_off);
+          a.q_M = q.Mq;
+          a.q_S = q.Sq;
+          a.k_M = k.Mq;
+          a.k_S = k.Sq;
+        }
         e = launch_attention(a, st);
         break;
       }
@@ -1176,6 +1215,7 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
         break;
       }
       case SK::RopeGroup: {
+        if (M == 1 && x.folded && !s->keep) return 0;  // done by the decode attention
         const Step& q = x.parts[0];
         const Step& k = x.parts[1];
         const Step& v = x.parts[2];
@@ -1953,20 +1993,23 @@ llx_status llx_profile_decode(llx_session* s, int pos, int iters, float* ms, dou
       } else {
         b = output_argmax_fused(m, R) ? 12.0 * R : 2.0 * R * m->vocab_padded + 4.0 * R;
       }
-      // one untimed launch, then `iters` timed launches
+      // one untimed launch, then `iters` timed launches; a step folded into a neighbour
+      // (it launches nothing at M = 1) reports zero time and zero bytes
+      int launched = 1;
       for (int it = 0; it <= iters; ++it) {
         if (it == 1) LLX_CUDA(cudaEventRecord(e0, s->st));
         if (i < (int)m->steps.size()) {
-          enqueue_steps(s, bd, i, i + 1, R, 1);
+          launched = enqueue_steps(s, bd, i, i + 1, R, 1);
         } else {
           launch_output_argmax(s, bd.p[m->output_act], R);
         }
       }
+      if (launched == 0) b = o = 0;
       LLX_CUDA(cudaEventRecord(e1, s->st));
       LLX_CUDA(cudaEventSynchronize(e1));
       float t = 0;
       LLX_CUDA(cudaEventElapsedTime(&t, e0, e1));
-      ms[i] = t / iters;
+      ms[i] = launched ? t / iters : 0.0f;
       bytes[i] = b;
       ops[i] = o;
     }
