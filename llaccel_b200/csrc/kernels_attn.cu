@@ -14,6 +14,7 @@
 #include <map>
 #include <mutex>
 #include <tuple>
+#include <type_traits>
 
 #include "kernels.h"
 #include "launch.cuh"
@@ -140,9 +141,11 @@ __global__ void k_attention(const int8_t* __restrict__ q, const int8_t* __restri
 // ---------------------------------------------------------------------------------------
 constexpr int kDecThreads = 256, kDecWarps = kDecThreads / 32;
 
-// KV tiles of 8 KB stream through a ring of kRing shared-memory stages.
 constexpr int kRing = 4;
-__host__ __device__ constexpr int dec_tile_keys(int D) { return 8192 / D; }
+// KV tiles of 8 KB (D <= 64) or 16 KB (D >= 128) stream through a ring of kRing stages;
+// at D >= 128 a tile has kDecThreads / dec_tpk(D) keys and dec_tpk(D) threads share a key.
+__host__ __device__ constexpr int dec_tile_keys(int D) { return (D >= 128 ? 16384 : 8192) / D; }
+__host__ __device__ constexpr int dec_tpk(int D) { return D >= 128 ? kDecThreads / dec_tile_keys(D) : 1; }
 
 // query heads per CTA: a KV head's H/Hkv query heads in groups of at most 8
 __host__ __device__ constexpr int dec_heads_per_cta(int rep) { return rep < 8 ? rep : 8; }
@@ -245,6 +248,8 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
     const uint16_t* __restrict__ luts, int32_t* err, int C, const AttnArgs rope) {
   constexpr int D = LPK * 16;
   constexpr int TK = dec_tile_keys(D);
+  constexpr int TPK = dec_tpk(D);
+  static_assert(TPK == 1 || TK * TPK == kDecThreads, "one key per TPK threads");
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ uint16_t s_expi[16], s_expf[256];
   __shared__ __align__(8) uint64_t full_bar[kRing];
@@ -377,26 +382,60 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
     patch(i);
     const int8_t* tile = ring + (size_t)(i % kRing) * TK * D;
     const int lt0 = i * TK, nk = min(TK, nkeys - lt0);
-    for (int l = threadIdx.x; l < nk; l += kDecThreads) {
+    if (TPK == 1) {
+      for (int l = threadIdx.x; l < nk; l += kDecThreads) {
+        const int8_t* krow = tile + (size_t)l * D;
+        int sv[RB];
+#pragma unroll
+        for (int r = 0; r < RB; ++r) sv[r] = 0;
+#pragma unroll
+        for (int cc = 0; cc < LPK; ++cc) {
+          // rotate the starting chunk by key so a warp's 32 rows spread over the banks
+          const int c = (cc + l) % LPK;
+          const uint4 kk = reinterpret_cast<const uint4*>(krow)[c];
+#pragma unroll
+          for (int r = 0; r < RB; ++r)
+            if (r < rep) sv[r] = dot16_i8(kk, reinterpret_cast<const uint4*>(q_s + r * D)[c], sv[r]);
+        }
+#pragma unroll
+        for (int r = 0; r < RB; ++r)
+          if (r < rep) {
+            mxl[r] = max(mxl[r], sv[r]);
+            sc[r * cap + lt0 + l] = sv[r];
+          }
+      }
+    } else {
+      // TPK threads per key, each LPK / TPK 16-byte chunks; the tile has exactly one key per
+      // TPK threads, so every thread takes part in the pair / quad reduction
+      constexpr int CPT = LPK / TPK;
+      const int l = threadIdx.x / TPK, sub = threadIdx.x % TPK;
+      const bool valid = l < nk;
       const int8_t* krow = tile + (size_t)l * D;
       int sv[RB];
 #pragma unroll
       for (int r = 0; r < RB; ++r) sv[r] = 0;
+      if (valid) {
 #pragma unroll
-      for (int cc = 0; cc < LPK; ++cc) {
-        // rotate the starting chunk by key so a warp's 32 rows spread over the banks
-        const int c = (cc + l) % LPK;
-        const uint4 kk = reinterpret_cast<const uint4*>(krow)[c];
+        for (int cc = 0; cc < CPT; ++cc) {
+          const int c = sub * CPT + (cc + l) % CPT;
+          const uint4 kk = reinterpret_cast<const uint4*>(krow)[c];
 #pragma unroll
-        for (int r = 0; r < RB; ++r)
-          if (r < rep) sv[r] = dot16_i8(kk, reinterpret_cast<const uint4*>(q_s + r * D)[c], sv[r]);
+          for (int r = 0; r < RB; ++r)
+            if (r < rep) sv[r] = dot16_i8(kk, reinterpret_cast<const uint4*>(q_s + r * D)[c], sv[r]);
+        }
       }
 #pragma unroll
-      for (int r = 0; r < RB; ++r)
-        if (r < rep) {
-          mxl[r] = max(mxl[r], sv[r]);
-          sc[r * cap + lt0 + l] = sv[r];
-        }
+      for (int o = 1; o < TPK; o <<= 1)
+#pragma unroll
+        for (int r = 0; r < RB; ++r) sv[r] += __shfl_xor_sync(0xffffffffu, sv[r], o);
+      if (valid && sub == 0) {
+#pragma unroll
+        for (int r = 0; r < RB; ++r)
+          if (r < rep) {
+            mxl[r] = max(mxl[r], sv[r]);
+            sc[r * cap + lt0 + l] = sv[r];
+          }
+      }
     }
     __syncthreads();  // stage consumed by every thread
     if (threadIdx.x == 0 && i + kRing < 2 * ntile) issue(i + kRing);
@@ -496,14 +535,23 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
     }
   }
   __syncthreads();
-  // ---- V slice: unit u = (head j, 4 channels) accumulates over the slice's keys in pairs ----
+  // ---- V slice: item = (key phase, unit u = (head j, 4 channels)) over key pairs ----
+  // A long slice splits each unit's key pairs into KS phases (the phase is the slow index,
+  // so a warp reads neighbouring channels of the same key rows); the phase sums meet in
+  // opart through shared-memory atomic adds (integer: exact in any order).
   constexpr int D4 = D / 4;
+  const int units = rep * D4;
+  int KS = 1;
+  if (nkeys > 512)
+    while (KS < 8 && units * KS * 2 <= kDecThreads) KS *= 2;
+  const int items = units * KS;
+  if (KS > 1)
+    for (int i = threadIdx.x; i < rep * D; i += kDecThreads) opart[i] = 0;
   int32_t acc[2][4];
 #pragma unroll
   for (int x = 0; x < 2; ++x)
 #pragma unroll
     for (int k = 0; k < 4; ++k) acc[x][k] = 0;
-  const int units = rep * D4;
   for (int i = ntile; i < 2 * ntile; ++i) {
     if (!wait_stage(i)) break;
     patch(i);
@@ -511,31 +559,51 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
     const int lt0 = (i - ntile) * TK, nk = min(TK, nkeys - lt0);
 #pragma unroll
     for (int x = 0; x < 2; ++x) {
-      const int u = threadIdx.x + x * kDecThreads;
-      if (u >= units) break;
+      const int it = threadIdx.x + x * kDecThreads;
+      if (it >= items) break;
+      const int ph = it / units, u = it % units;
       const int j = u / D4, c4 = (u % D4) * 4;
       const int16_t* pj = pn16 + (size_t)j * cap + lt0;
-      for (int l = 0; l < nk; l += 2) {
-        // the row after the last key may be stale shared memory: its pn is 0
-        const uint32_t va = *reinterpret_cast<const uint32_t*>(tile + (size_t)l * D + c4);
-        const uint32_t vb = *reinterpret_cast<const uint32_t*>(tile + (size_t)(l + 1) * D + c4);
-        const int pp = *reinterpret_cast<const int*>(pj + l);
-        const uint32_t lo = __byte_perm(va, vb, 0x5140), hi = __byte_perm(va, vb, 0x7362);
-        acc[x][0] = __dp2a_lo(pp, (int)lo, acc[x][0]);
-        acc[x][1] = __dp2a_hi(pp, (int)lo, acc[x][1]);
-        acc[x][2] = __dp2a_lo(pp, (int)hi, acc[x][2]);
-        acc[x][3] = __dp2a_hi(pp, (int)hi, acc[x][3]);
+      // key pairs l, l + 1 with a compile-time stride per phase count
+      auto pairs = [&](auto ks) {
+        constexpr int KSC = decltype(ks)::value;
+        for (int l = 2 * ph; l < nk; l += 2 * KSC) {
+          // the row after the last key may be stale shared memory: its pn is 0
+          const uint32_t va = *reinterpret_cast<const uint32_t*>(tile + (size_t)l * D + c4);
+          const uint32_t vb = *reinterpret_cast<const uint32_t*>(tile + (size_t)(l + 1) * D + c4);
+          const int pp = *reinterpret_cast<const int*>(pj + l);
+          const uint32_t lo = __byte_perm(va, vb, 0x5140), hi = __byte_perm(va, vb, 0x7362);
+          acc[x][0] = __dp2a_lo(pp, (int)lo, acc[x][0]);
+          acc[x][1] = __dp2a_hi(pp, (int)lo, acc[x][1]);
+          acc[x][2] = __dp2a_lo(pp, (int)hi, acc[x][2]);
+          acc[x][3] = __dp2a_hi(pp, (int)hi, acc[x][3]);
+        }
+      };
+      switch (KS) {
+        case 1: pairs(std::integral_constant<int, 1>{}); break;
+        case 2: pairs(std::integral_constant<int, 2>{}); break;
+        case 4: pairs(std::integral_constant<int, 4>{}); break;
+        default: pairs(std::integral_constant<int, 8>{}); break;
       }
     }
     __syncthreads();  // stage consumed by every thread
     if (threadIdx.x == 0 && i + kRing < 2 * ntile) issue(i + kRing);
   }
+  if (KS > 1) __syncthreads();  // opart zeroed by every thread before any adds
 #pragma unroll
   for (int x = 0; x < 2; ++x) {
-    const int u = threadIdx.x + x * kDecThreads;
-    if (u < units)
+    const int it = threadIdx.x + x * kDecThreads;
+    if (it < items) {
+      const int u = it % units;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) opart[(u / D4) * D + (u % D4) * 4 + k] = acc[x][k];
+      for (int k = 0; k < 4; ++k) {
+        int32_t* dst = &opart[(u / D4) * D + (u % D4) * 4 + k];
+        if (KS > 1)
+          atomicAdd(dst, acc[x][k]);
+        else
+          *dst = acc[x][k];
+      }
+    }
   }
   // ---- exchange 3: slice value sums -> outputs; CTA `crank` finishes outputs idx = crank mod C ----
   dec_cluster_sync();
