@@ -477,17 +477,31 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
       mx[j] = j < rep ? s_gmax[j] : 0;
       sum[j] = 0;
     }
-    if (live)
+    // the exp-LUT gap: for Ss >= 33 from the product's high word (gap_prob_hi), chosen once
+    // for the whole pass so the unrolled loop stays branch-free
+    auto exp_pass = [&](auto fast) {
+      constexpr bool FAST = decltype(fast)::value;
+      const uint32_t rnd = FAST ? 1u << (Ss - 33) : 0u;
+      const int zsh = FAST ? Ss - 32 : 0;
       for (int t = threadIdx.x; t < nkeys; t += kDecThreads) {
 #pragma unroll
         for (int j = 0; j < RB; ++j) {
           if (j < rep) {
-            const uint32_t pr = gap_prob((uint32_t)(mx[j] - sc[j * cap + t]), (uint32_t)Ms, Ss, s_expi, s_expf);
+            const uint32_t d = (uint32_t)(mx[j] - sc[j * cap + t]);
+            const uint32_t pr = FAST ? gap_prob_hi(d, (uint32_t)Ms, rnd, zsh, s_expi, s_expf)
+                                     : gap_prob(d, (uint32_t)Ms, Ss, s_expi, s_expf);
             sc[j * cap + t] = (int32_t)pr;
             sum[j] += pr;
           }
         }
       }
+    };
+    if (live) {
+      if (Ss >= 33)
+        exp_pass(std::true_type{});
+      else
+        exp_pass(std::false_type{});
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
