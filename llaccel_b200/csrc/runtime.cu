@@ -1315,6 +1315,14 @@ static void plan_arena(llx_session* s) {
       for (int a : step_ins(x)) last[a] = std::max(last[a], i);
     }
     last[m->output_act] = ns;
+    // a decode attention with its RoPE group folded in reads that group's inputs (q and k
+    // before rotation, v): they live through the attention step, so its output never
+    // takes their memory while other CTAs still read them
+    for (int i = 0; i < ns; ++i) {
+      const Step& x = m->steps[i];
+      if (x.kind != SK::Attention || x.rope_step < 0) continue;
+      for (int a : step_ins(m->steps[x.rope_step])) last[a] = std::max(last[a], i);
+    }
     for (size_t a = 0; a < na; ++a) last[a] = std::max(last[a], def[a]);
     for (int i = 0; i <= ns; ++i) {
       for (size_t a = 0; a < na; ++a)

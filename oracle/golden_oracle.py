@@ -215,18 +215,28 @@ def attention_rows(q, kc, vc, H, Hkv, D, pos, Ms, Ss, Mo, So, prob_bits=8):
         kvh = h // rep
         K = kc[kvh, :Tm].astype(I64)
         V = vc[kvh, :Tm].astype(I64)
-        s = q[:, h * D : (h + 1) * D] @ K.T
+        s = _exact_product(q[:, h * D : (h + 1) * D], K.T)
         mx = np.where(valid, s, np.iinfo(np.int64).min).max(axis=1, keepdims=True)
         z = mulshift(np.where(valid, mx - s, 0), Ms, Ss)
         p = np.where(valid, _probs(z), 0)
         tot = p.sum(axis=1)
         inv = np.array([udiv(1 << 31, int(t)) for t in tot], dtype=I64)[:, None]
         pn = np.minimum(rshr(p * inv, 31 - prob_bits), (1 << prob_bits) - 1)
-        o = pn @ V
+        o = _exact_product(pn, V)
         if prob_bits == 15:
             o = rshr(o, 7)
         out[:, h * D : (h + 1) * D] = sat8(mulshift(o, Mo, So))
     return out
+
+
+def _exact_product(a, b):
+    """Integer a @ b, through float64 when every partial sum is below 2^53 (q.k: int8 x int8
+    over D; p.v: p < 2^15 times int8 over the keys), else in int64."""
+    amax = int(np.abs(a).max(initial=0))
+    bmax = int(np.abs(b).max(initial=0))
+    if amax * bmax * a.shape[1] < 1 << 53:
+        return (a.astype(np.float64) @ b.astype(np.float64)).astype(I64)
+    return a @ b
 
 
 def exact_matmul(a, w):

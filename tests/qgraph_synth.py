@@ -31,7 +31,7 @@ class _Blob:
 
 
 def build(out: Path, *, dim=64, n_layers=2, H=4, Hkv=2, D=32, ffn=96, vocab=40, max_seq=64, fuse=True, seed=0,
-          qk_norm=False, bias=True, prob_bits=15, extreme=False, prefill_m=16) -> Path:
+          qk_norm=False, bias=True, prob_bits=15, extreme=False, prefill_m=16, att_S=(28, 41)) -> Path:
     rng = np.random.default_rng(seed)
     vp = (vocab + 15) // 16 * 16
     blob = _Blob()
@@ -97,7 +97,7 @@ def build(out: Path, *, dim=64, n_layers=2, H=4, Hkv=2, D=32, ffn=96, vocab=40, 
         qq, kq = quant(f"{p}.qr"), quant(f"{p}.kr")
         ops.append({"op": "kv_write", "layer": i, "k": kq, "v": f"{p}.v", "Hkv": Hkv, "D": D})
         ops.append({"op": "attention", "q": qq, "layer": i, "out": f"{p}.a", "H": H, "Hkv": Hkv, "D": D,
-                    "Ms": int(rng.integers(1 << 30, 1 << 31)), "Ss": int(rng.integers(28, 41)),
+                    "Ms": int(rng.integers(1 << 30, 1 << 31)), "Ss": int(rng.integers(*att_S)),
                     "Mo": int(rng.integers(1 << 30, 1 << 31)), "So": int(rng.integers(36, 40)),
                     "prob_bits": prob_bits})
         silu = {"Mi": int(rng.integers(1 << 30, 1 << 32)), "Si": int(rng.integers(28, 38)),
