@@ -141,9 +141,11 @@ __global__ void k_attention(const int8_t* __restrict__ q, const int8_t* __restri
 // ---------------------------------------------------------------------------------------
 constexpr int kDecThreads = 256, kDecWarps = kDecThreads / 32;
 
-constexpr int kRing = 4;
 // KV tiles of 8 KB (D <= 64) or 16 KB (D >= 128) stream through a ring of kRing stages;
 // at D >= 128 a tile has kDecThreads / dec_tpk(D) keys and dec_tpk(D) threads share a key.
+// Three stages keep 3 CTAs per SM resident at head dim 128 (with four, shared memory held 2,
+// and at 8 waves of short slices per layer the per-CTA latency chains went unhidden).
+constexpr int kRing = 3;
 __host__ __device__ constexpr int dec_tile_keys(int D) { return (D >= 128 ? 16384 : 8192) / D; }
 __host__ __device__ constexpr int dec_tpk(int D) { return D >= 128 ? kDecThreads / dec_tile_keys(D) : 1; }
 
@@ -153,9 +155,25 @@ __host__ __device__ constexpr int dec_heads_per_cta(int rep) { return rep < 8 ? 
 // keys per CTA slice (capacity) for cluster size C: ceil(max_seq / C) + a zero pad entry
 __host__ __device__ constexpr int dec_slice_cap(int max_seq, int C) { return ((max_seq + C - 1) / C + 2) & ~1; }
 
+// CTAs of RB query heads at head dim D run the score and value passes on int8 tensor-core
+// tiles (mma m16n8k32, 8 head columns): with 4 or more heads per CTA; at 1 or 2 heads most
+// of the tile is padding and the CUDA-core passes are faster (measured at head dim 128)
+__host__ __device__ constexpr bool dec_tc(int D, int RB) { return (D == 64 || D == 128) && RB >= 4; }
+// row stride (bytes) of the hi / lo probability planes of the tensor-core value pass: whole
+// tiles of the largest slice plus 16 bytes, so the 8 head rows of a fragment load fall in
+// different banks
+__host__ __device__ constexpr int dec_prow(int max_seq, int C, int TK) {
+  return ((max_seq + C - 1) / C + TK - 1) / TK * TK + 16;
+}
+// bytes of the probability region: normalised p as i16 [RB][cap], or the hi / lo u8 planes
+static size_t dec_p_bytes(int RB, int D, int max_seq, int C) {
+  const size_t cap = (size_t)dec_slice_cap(max_seq, C);
+  return dec_tc(D, RB) ? (size_t)2 * RB * dec_prow(max_seq, C, dec_tile_keys(D)) : (size_t)RB * cap * 2;
+}
+
 static size_t dec_smem_bytes(int RB, int D, int max_seq, int C) {
   const size_t cap = (size_t)dec_slice_cap(max_seq, C);
-  return (size_t)kRing * dec_tile_keys(D) * D + (size_t)RB * D + (size_t)RB * cap * 4 + (size_t)RB * cap * 2 +
+  return (size_t)kRing * dec_tile_keys(D) * D + (size_t)RB * D + (size_t)RB * cap * 4 + dec_p_bytes(RB, D, max_seq, C) +
          (size_t)RB * D * 4 + (size_t)kDecWarps * RB * 4 + (size_t)2 * RB * 4 + 128;
 }
 
@@ -241,6 +259,31 @@ __device__ __forceinline__ uint32_t dec_peer_u32(const void* local, uint32_t ran
   return v;
 }
 
+// d += a (16x32, s8) x b (32x8, s8, or u8 when B_U8): one m16n8k32 integer tensor-core tile
+template <bool B_U8>
+__device__ __forceinline__ void dec_mma(int32_t (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+  if (B_U8)
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// 4 x 4 byte transpose: x_e holds channels 0..3 of key e; w[q] gets channel q of keys 0..3
+__device__ __forceinline__ void dec_transpose4(uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3, uint32_t* w) {
+  const uint32_t t0 = __byte_perm(x0, x1, 0x5140), t1 = __byte_perm(x0, x1, 0x7362);
+  const uint32_t t2 = __byte_perm(x2, x3, 0x5140), t3 = __byte_perm(x2, x3, 0x7362);
+  w[0] = __byte_perm(t0, t2, 0x5410);
+  w[1] = __byte_perm(t0, t2, 0x7632);
+  w[2] = __byte_perm(t1, t3, 0x5410);
+  w[3] = __byte_perm(t1, t3, 0x7632);
+}
+
 template <int LPK, int RB>
 __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
     const int8_t* __restrict__ q, const int8_t* __restrict__ kc, const int8_t* __restrict__ vc, int8_t* __restrict__ out,
@@ -264,8 +307,14 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   int8_t* ring = reinterpret_cast<int8_t*>(smem);                        // [kRing][TK][D]
   int8_t* q_s = ring + (size_t)kRing * TK * D;                           // [RB][D]
   int32_t* sc = reinterpret_cast<int32_t*>(q_s + RB * D);                // [RB][cap] scores, then p
-  int16_t* pn16 = reinterpret_cast<int16_t*>(sc + (size_t)RB * cap);      // [RB][cap] normalised p
-  int32_t* opart = reinterpret_cast<int32_t*>(pn16 + (size_t)RB * cap);   // [RB][D] this slice's value sums
+  // normalised p: i16 [RB][cap], or (tensor-core value pass) hi / lo u8 planes [RB][prow]
+  constexpr bool TC = dec_tc(D, RB);
+  const int prow = dec_prow(max_seq, C, TK);
+  int16_t* pn16 = reinterpret_cast<int16_t*>(sc + (size_t)RB * cap);
+  uint8_t* p_hi = reinterpret_cast<uint8_t*>(pn16);
+  uint8_t* p_lo = p_hi + (size_t)RB * prow;
+  int32_t* opart = reinterpret_cast<int32_t*>(reinterpret_cast<unsigned char*>(pn16) +
+                                              (TC ? (size_t)2 * RB * prow : (size_t)RB * cap * 2));  // [RB][D]
   int32_t* wred = opart + RB * D;                                        // [warps][RB]
   int32_t* xmax = wred + kDecWarps * RB;                                 // [RB] slice maxima (read by peers)
   uint32_t* xsum = reinterpret_cast<uint32_t*>(xmax + RB);               // [RB] slice sums (read by peers)
@@ -377,12 +426,60 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   int32_t mxl[RB];
 #pragma unroll
   for (int j = 0; j < RB; ++j) mxl[j] = INT_MIN;
+  // tensor-core score pass: S^T (16 keys x 8 heads) = K (16 x 32 channels) Q^T per MMA.  The
+  // MMA's k index 4 tig + e (e < 4) is channel 8 tig + e of the 32-channel block and k index
+  // 16 + 4 tig + e is channel 8 tig + 4 + e, so a thread's A and B operands of one block are
+  // one 8-byte load each.  Thread (g, tig) keeps Q^T columns of head g; its results are the
+  // scores of heads 2 tig and 2 tig + 1 (running maxima mxa, mxb).
+  const int g = lane >> 2, tig = lane & 3, h0 = 2 * tig, h1 = 2 * tig + 1;
+  int32_t mxa = INT_MIN, mxb = INT_MIN;
+  uint2 qf[TC ? D / 32 : 1];
+  if constexpr (TC) {
+    __syncthreads();  // q_s complete
+#pragma unroll
+    for (int kb = 0; kb < D / 32; ++kb)
+      qf[kb] = g < rep ? *reinterpret_cast<const uint2*>(q_s + g * D + kb * 32 + 8 * tig) : make_uint2(0u, 0u);
+  }
   for (int i = 0; i < ntile; ++i) {
     if (!wait_stage(i)) break;
     patch(i);
     const int8_t* tile = ring + (size_t)(i % kRing) * TK * D;
     const int lt0 = i * TK, nk = min(TK, nkeys - lt0);
-    if (TPK == 1) {
+    if constexpr (TC) {
+      static_assert(TK / 16 == kDecWarps, "one 16-key block per warp and tile");
+      const int r = warp * 16 + g;  // tile rows r and r + 8 (rows past nk are stale, never stored)
+      if (warp * 16 < nk) {
+        const int8_t* r0 = tile + (size_t)r * D + 8 * tig;
+        const int8_t* r1 = r0 + 8 * D;
+        int32_t c[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int kb = 0; kb < D / 32; ++kb) {
+          const uint2 x0 = *reinterpret_cast<const uint2*>(r0 + kb * 32);
+          const uint2 x1 = *reinterpret_cast<const uint2*>(r1 + kb * 32);
+          dec_mma<false>(c, x0.x, x1.x, x0.y, x1.y, qf[kb].x, qf[kb].y);
+        }
+        if (r < nk) {
+          if (h0 < rep) {
+            sc[h0 * cap + lt0 + r] = c[0];
+            mxa = max(mxa, c[0]);
+          }
+          if (h1 < rep) {
+            sc[h1 * cap + lt0 + r] = c[1];
+            mxb = max(mxb, c[1]);
+          }
+        }
+        if (r + 8 < nk) {
+          if (h0 < rep) {
+            sc[h0 * cap + lt0 + r + 8] = c[2];
+            mxa = max(mxa, c[2]);
+          }
+          if (h1 < rep) {
+            sc[h1 * cap + lt0 + r + 8] = c[3];
+            mxb = max(mxb, c[3]);
+          }
+        }
+      }
+    } else if (TPK == 1) {
       for (int l = threadIdx.x; l < nk; l += kDecThreads) {
         const int8_t* krow = tile + (size_t)l * D;
         int sv[RB];
@@ -441,12 +538,24 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
     if (threadIdx.x == 0 && i + kRing < 2 * ntile) issue(i + kRing);
   }
   // ---- exchange 1: slice maxima -> global per-head max ----
+  if constexpr (TC) {
 #pragma unroll
-  for (int j = 0; j < RB; ++j) {
-    int32_t v = mxl[j];
+    for (int o = 4; o < 32; o <<= 1) {
+      mxa = max(mxa, __shfl_xor_sync(0xffffffffu, mxa, o));
+      mxb = max(mxb, __shfl_xor_sync(0xffffffffu, mxb, o));
+    }
+    if (g == 0) {
+      if (h0 < RB) wred[warp * RB + h0] = mxa;
+      if (h1 < RB) wred[warp * RB + h1] = mxb;
+    }
+  } else {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
-    if (lane == 0) wred[warp * RB + j] = v;
+    for (int j = 0; j < RB; ++j) {
+      int32_t v = mxl[j];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+      if (lane == 0) wred[warp * RB + j] = v;
+    }
   }
   __syncthreads();
   if (threadIdx.x < RB) {
@@ -534,88 +643,189 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   // p <= sum, so p * inv <= 2^31: the product and its rounding shift stay in 32 bits
   const uint32_t pmax = (1u << prob_bits) - 1u;
   const int pshift = 31 - prob_bits;
-  for (int j = 0; j < rep; ++j) {
-    const uint32_t inv = s_inv[j];
-    const int32_t* sj = sc + j * cap;
-    int16_t* pj = pn16 + (size_t)j * cap;
-    for (int t = threadIdx.x; t < cap; t += kDecThreads) {
-      uint32_t v = 0;
-      if (t < nkeys && live) {
-        const uint32_t x = (uint32_t)sj[t] * inv;
-        const uint32_t pn = (x >> pshift) + ((x >> (pshift - 1)) & 1u);
-        v = pn < pmax ? pn : pmax;
+  if constexpr (TC) {
+    // hi / lo bytes of pn (pn < 2^15) for the value MMAs, over whole tiles (0 past the
+    // slice).  Within each 16-key half the value pass's MMA k index 4 tig + e stands for key
+    // 4 e + tig, so key u of a half is stored at 4 (u % 4) + u / 4: a thread's 4 keys are
+    // one 4-byte load.
+    const int nfill = ntile * TK;
+    for (int j = 0; j < rep; ++j) {
+      const uint32_t inv = s_inv[j];
+      const int32_t* sj = sc + j * cap;
+      for (int t = threadIdx.x; t < nfill; t += kDecThreads) {
+        uint32_t v = 0;
+        if (t < nkeys && live) {
+          const uint32_t x = (uint32_t)sj[t] * inv;
+          const uint32_t pn = (x >> pshift) + ((x >> (pshift - 1)) & 1u);
+          v = pn < pmax ? pn : pmax;
+        }
+        const int u = t & 15, at = j * prow + (t & ~15) + 4 * (u & 3) + (u >> 2);
+        p_hi[at] = (uint8_t)(v >> 8);
+        p_lo[at] = (uint8_t)(v & 255u);
       }
-      pj[t] = (int16_t)v;  // entries past the slice stay 0: they weight the stale pair row
+    }
+  } else {
+    for (int j = 0; j < rep; ++j) {
+      const uint32_t inv = s_inv[j];
+      const int32_t* sj = sc + j * cap;
+      int16_t* pj = pn16 + (size_t)j * cap;
+      for (int t = threadIdx.x; t < cap; t += kDecThreads) {
+        uint32_t v = 0;
+        if (t < nkeys && live) {
+          const uint32_t x = (uint32_t)sj[t] * inv;
+          const uint32_t pn = (x >> pshift) + ((x >> (pshift - 1)) & 1u);
+          v = pn < pmax ? pn : pmax;
+        }
+        pj[t] = (int16_t)v;  // entries past the slice stay 0: they weight the stale pair row
+      }
     }
   }
   __syncthreads();
-  // ---- V slice: item = (key phase, unit u = (head j, 4 channels)) over key pairs ----
-  // A long slice splits each unit's key pairs into KS phases (the phase is the slow index,
-  // so a warp reads neighbouring channels of the same key rows); the phase sums meet in
-  // opart through shared-memory atomic adds (integer: exact in any order).
-  constexpr int D4 = D / 4;
-  const int units = rep * D4;
-  int KS = 1;
-  if (nkeys > 512)
-    while (KS < 8 && units * KS * 2 <= kDecThreads) KS *= 2;
-  const int items = units * KS;
-  if (KS > 1)
+  if constexpr (TC) {
+    // ---- tensor-core value pass: O^T (16 channels x 8 heads) += V^T (16 x 32 keys) P^T ----
+    // Warp w takes the 32-key chunk w % 4 of every tile and half w / 4 of the channels.  In
+    // its m-block m, row g stands for channel g D/8 + half D/16 + 2 m and row g + 8 for the
+    // next channel, so thread (g, tig) reads D/16 contiguous bytes of each of its 8 key rows
+    // (keys 4 e + tig and 16 + 4 e + tig of the chunk) and transposes them into the A
+    // operand.  pn enters as two unsigned bytes, O = 256 (hi V) + (lo V), exact in int32;
+    // the hi MMAs are skipped when pn has 8 bits.  The warps' sums meet in opart through
+    // shared-memory atomic adds (integer: exact in any order).
+    constexpr int CW = D / 16, MBH = D / 32;
+    const int kc = warp & 3, half = warp >> 2;
+    const bool wide = prob_bits > 8;
     for (int i = threadIdx.x; i < rep * D; i += kDecThreads) opart[i] = 0;
-  int32_t acc[2][4];
+    int32_t ah[MBH][4], al[MBH][4];
 #pragma unroll
-  for (int x = 0; x < 2; ++x)
+    for (int m = 0; m < MBH; ++m)
 #pragma unroll
-    for (int k = 0; k < 4; ++k) acc[x][k] = 0;
-  for (int i = ntile; i < 2 * ntile; ++i) {
-    if (!wait_stage(i)) break;
-    patch(i);
-    const int8_t* tile = ring + (size_t)(i % kRing) * TK * D;
-    const int lt0 = (i - ntile) * TK, nk = min(TK, nkeys - lt0);
+      for (int k = 0; k < 4; ++k) ah[m][k] = al[m][k] = 0;
+    for (int i = ntile; i < 2 * ntile; ++i) {
+      if (!wait_stage(i)) break;
+      patch(i);
+      const int8_t* tile = ring + (size_t)(i % kRing) * TK * D;
+      const int lt0 = (i - ntile) * TK, nk = min(TK, nkeys - lt0);
+      if (kc * 32 < nk) {  // rows past nk are stale shared memory; their pn bytes are 0
+        const int8_t* vrow = tile + (size_t)(kc * 32 + tig) * D + g * (D / 8) + half * CW;
+        uint32_t wa[CW], wb[CW];
+        if constexpr (CW == 8) {
+          uint2 xa[4], xb[4];
 #pragma unroll
-    for (int x = 0; x < 2; ++x) {
-      const int it = threadIdx.x + x * kDecThreads;
-      if (it >= items) break;
-      const int ph = it / units, u = it % units;
-      const int j = u / D4, c4 = (u % D4) * 4;
-      const int16_t* pj = pn16 + (size_t)j * cap + lt0;
-      // key pairs l, l + 1 with a compile-time stride per phase count
-      auto pairs = [&](auto ks) {
-        constexpr int KSC = decltype(ks)::value;
-        for (int l = 2 * ph; l < nk; l += 2 * KSC) {
-          // the row after the last key may be stale shared memory: its pn is 0
-          const uint32_t va = *reinterpret_cast<const uint32_t*>(tile + (size_t)l * D + c4);
-          const uint32_t vb = *reinterpret_cast<const uint32_t*>(tile + (size_t)(l + 1) * D + c4);
-          const int pp = *reinterpret_cast<const int*>(pj + l);
-          const uint32_t lo = __byte_perm(va, vb, 0x5140), hi = __byte_perm(va, vb, 0x7362);
-          acc[x][0] = __dp2a_lo(pp, (int)lo, acc[x][0]);
-          acc[x][1] = __dp2a_hi(pp, (int)lo, acc[x][1]);
-          acc[x][2] = __dp2a_lo(pp, (int)hi, acc[x][2]);
-          acc[x][3] = __dp2a_hi(pp, (int)hi, acc[x][3]);
+          for (int e = 0; e < 4; ++e) {
+            xa[e] = *reinterpret_cast<const uint2*>(vrow + (size_t)(4 * e) * D);
+            xb[e] = *reinterpret_cast<const uint2*>(vrow + (size_t)(16 + 4 * e) * D);
+          }
+          dec_transpose4(xa[0].x, xa[1].x, xa[2].x, xa[3].x, wa);
+          dec_transpose4(xa[0].y, xa[1].y, xa[2].y, xa[3].y, wa + 4);
+          dec_transpose4(xb[0].x, xb[1].x, xb[2].x, xb[3].x, wb);
+          dec_transpose4(xb[0].y, xb[1].y, xb[2].y, xb[3].y, wb + 4);
+        } else {
+          uint32_t xa[4], xb[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            xa[e] = *reinterpret_cast<const uint32_t*>(vrow + (size_t)(4 * e) * D);
+            xb[e] = *reinterpret_cast<const uint32_t*>(vrow + (size_t)(16 + 4 * e) * D);
+          }
+          dec_transpose4(xa[0], xa[1], xa[2], xa[3], wa);
+          dec_transpose4(xb[0], xb[1], xb[2], xb[3], wb);
         }
-      };
-      switch (KS) {
-        case 1: pairs(std::integral_constant<int, 1>{}); break;
-        case 2: pairs(std::integral_constant<int, 2>{}); break;
-        case 4: pairs(std::integral_constant<int, 4>{}); break;
-        default: pairs(std::integral_constant<int, 8>{}); break;
-      }
-    }
-    __syncthreads();  // stage consumed by every thread
-    if (threadIdx.x == 0 && i + kRing < 2 * ntile) issue(i + kRing);
-  }
-  if (KS > 1) __syncthreads();  // opart zeroed by every thread before any adds
+        uint32_t bl0 = 0, bl1 = 0, bh0 = 0, bh1 = 0;
+        if (g < rep) {
+          const int pb = g * prow + lt0 + kc * 32 + 4 * tig;
+          bl0 = *reinterpret_cast<const uint32_t*>(p_lo + pb);
+          bl1 = *reinterpret_cast<const uint32_t*>(p_lo + pb + 16);
+          if (wide) {
+            bh0 = *reinterpret_cast<const uint32_t*>(p_hi + pb);
+            bh1 = *reinterpret_cast<const uint32_t*>(p_hi + pb + 16);
+          }
+        }
 #pragma unroll
-  for (int x = 0; x < 2; ++x) {
-    const int it = threadIdx.x + x * kDecThreads;
-    if (it < items) {
-      const int u = it % units;
+        for (int m = 0; m < MBH; ++m) {
+          dec_mma<true>(al[m], wa[2 * m], wa[2 * m + 1], wb[2 * m], wb[2 * m + 1], bl0, bl1);
+          if (wide) dec_mma<true>(ah[m], wa[2 * m], wa[2 * m + 1], wb[2 * m], wb[2 * m + 1], bh0, bh1);
+        }
+      }
+      __syncthreads();  // stage consumed by every thread
+      if (threadIdx.x == 0 && i + kRing < 2 * ntile) issue(i + kRing);
+    }
+    __syncthreads();  // opart zeroed by every thread before any adds
+#pragma unroll
+    for (int m = 0; m < MBH; ++m) {
+      const int ch = g * (D / 8) + half * CW + 2 * m;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        int32_t* dst = &opart[(u / D4) * D + (u % D4) * 4 + k];
-        if (KS > 1)
-          atomicAdd(dst, acc[x][k]);
-        else
-          *dst = acc[x][k];
+        const int hd = 2 * tig + (k & 1), c = ch + (k >> 1);
+        if (hd < rep) atomicAdd(&opart[hd * D + c], ah[m][k] * 256 + al[m][k]);
+      }
+    }
+  } else {
+    // ---- V slice: item = (key phase, unit u = (head j, 4 channels)) over key pairs ----
+    // A long slice splits each unit's key pairs into KS phases (the phase is the slow index,
+    // so a warp reads neighbouring channels of the same key rows); the phase sums meet in
+    // opart through shared-memory atomic adds (integer: exact in any order).
+    constexpr int D4 = D / 4;
+    const int units = rep * D4;
+    int KS = 1;
+    if (nkeys > 512)
+      while (KS < 8 && units * KS * 2 <= kDecThreads) KS *= 2;
+    const int items = units * KS;
+    if (KS > 1)
+      for (int i = threadIdx.x; i < rep * D; i += kDecThreads) opart[i] = 0;
+    int32_t acc[2][4];
+  #pragma unroll
+    for (int x = 0; x < 2; ++x)
+  #pragma unroll
+      for (int k = 0; k < 4; ++k) acc[x][k] = 0;
+    for (int i = ntile; i < 2 * ntile; ++i) {
+      if (!wait_stage(i)) break;
+      patch(i);
+      const int8_t* tile = ring + (size_t)(i % kRing) * TK * D;
+      const int lt0 = (i - ntile) * TK, nk = min(TK, nkeys - lt0);
+  #pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        const int it = threadIdx.x + x * kDecThreads;
+        if (it >= items) break;
+        const int ph = it / units, u = it % units;
+        const int j = u / D4, c4 = (u % D4) * 4;
+        const int16_t* pj = pn16 + (size_t)j * cap + lt0;
+        // key pairs l, l + 1 with a compile-time stride per phase count
+        auto pairs = [&](auto ks) {
+          constexpr int KSC = decltype(ks)::value;
+          for (int l = 2 * ph; l < nk; l += 2 * KSC) {
+            // the row after the last key may be stale shared memory: its pn is 0
+            const uint32_t va = *reinterpret_cast<const uint32_t*>(tile + (size_t)l * D + c4);
+            const uint32_t vb = *reinterpret_cast<const uint32_t*>(tile + (size_t)(l + 1) * D + c4);
+            const int pp = *reinterpret_cast<const int*>(pj + l);
+            const uint32_t lo = __byte_perm(va, vb, 0x5140), hi = __byte_perm(va, vb, 0x7362);
+            acc[x][0] = __dp2a_lo(pp, (int)lo, acc[x][0]);
+            acc[x][1] = __dp2a_hi(pp, (int)lo, acc[x][1]);
+            acc[x][2] = __dp2a_lo(pp, (int)hi, acc[x][2]);
+            acc[x][3] = __dp2a_hi(pp, (int)hi, acc[x][3]);
+          }
+        };
+        switch (KS) {
+          case 1: pairs(std::integral_constant<int, 1>{}); break;
+          case 2: pairs(std::integral_constant<int, 2>{}); break;
+          case 4: pairs(std::integral_constant<int, 4>{}); break;
+          default: pairs(std::integral_constant<int, 8>{}); break;
+        }
+      }
+      __syncthreads();  // stage consumed by every thread
+      if (threadIdx.x == 0 && i + kRing < 2 * ntile) issue(i + kRing);
+    }
+    if (KS > 1) __syncthreads();  // opart zeroed by every thread before any adds
+  #pragma unroll
+    for (int x = 0; x < 2; ++x) {
+      const int it = threadIdx.x + x * kDecThreads;
+      if (it < items) {
+        const int u = it % units;
+  #pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          int32_t* dst = &opart[(u / D4) * D + (u % D4) * 4 + k];
+          if (KS > 1)
+            atomicAdd(dst, acc[x][k]);
+          else
+            *dst = acc[x][k];
+        }
       }
     }
   }

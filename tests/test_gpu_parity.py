@@ -255,12 +255,14 @@ def test_persistent_gated_prefill_matches_oracle(tmp_path):
         assert m.generate_batch(prompts, 4, prefill_rows=64) == want
 
 
-@pytest.mark.parametrize("D,H,Hkv,S", [(128, 8, 2, (37, 38)), (128, 8, 2, (42, 43)), (64, 14, 2, (34, 38))])
+@pytest.mark.parametrize("D,H,Hkv,S", [(128, 8, 2, (37, 38)), (128, 8, 2, (42, 43)), (64, 14, 2, (34, 38)),
+                                         (128, 4, 2, (40, 42))])
 def test_long_context_batch_decode_matches_oracle(tmp_path, D, H, Hkv, S):
     """Decode attention over long slices: 96 sequences give more (sequence, KV head) pairs
     than one wave of 4-CTA clusters holds, so each pair splits its 1200+ keys over 2 CTAs of
-    about 600: the value pass runs in key phases, and the newest row (RoPE folded into the
-    attention) lands in the last tile of the ring.  Ss spans a peaked and a flat softmax.
+    about 600, and the newest row (RoPE folded into the attention) lands in the last tile of
+    the ring.  4 and 7 query heads per KV head take the tensor-core passes, 2 the CUDA-core
+    passes with the value pass in key phases.  Ss spans a peaked and a flat softmax.
     Records equal the oracle's for every sequence, and a second run repeats them exactly."""
     L, n, B = 1200, 10, 96
     d = qgraph_synth.build(tmp_path / "g", dim=128, n_layers=1, H=H, Hkv=Hkv, D=D, ffn=64, vocab=40,
