@@ -53,10 +53,13 @@ __device__ __forceinline__ int dot16(const uint4& w, const uint4& x, int acc) {
 }
 
 // ---- GEMV: 8 channels per 256-thread block, RB rows per block row ------------------------
+// The weights are model constants: a thread's first four 16-byte weight loads are issued
+// before the grid dependency wait, so they stream while the previous kernel finishes.  Each
+// later round of four is requested together, before any of it is consumed (one buffer:
+// 38 registers keep 6 blocks per SM resident).
 template <int RB>
 __global__ void __launch_bounds__(256) k_gemv(LinearArgs a) {
   pdl_trigger();
-  pdl_wait();
   __shared__ int32_t part[8][8][RB];  // [warp][channel][row]
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = lane >> 2, sub = lane & 3;
@@ -64,31 +67,33 @@ __global__ void __launch_bounds__(256) k_gemv(LinearArgs a) {
   const int n0 = blockIdx.x * 8, r0 = blockIdx.y * RB;
   const int n = n0 + c;
   const int nk = a.K >> 4;
+  const bool live = n < a.N;
+  const uint4* wr = reinterpret_cast<const uint4*>(a.W + (int64_t)(live ? n : 0) * a.K);
+  auto fetch = [&](int k0, uint4 (&wv)[4]) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int k = k0 + 32 * u;
+      wv[u] = live && k < nk ? __ldcs(wr + k) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  uint4 cur[4];
+  fetch(slot, cur);
+  pdl_wait();  // the activation rows and the output buffer belong to earlier kernels
   int32_t acc[RB];
 #pragma unroll
   for (int i = 0; i < RB; ++i) acc[i] = 0;
-  if (n < a.N) {
-    // four independent 16-byte weight loads in flight per thread before any is consumed:
-    // the weights stream once per launch (HBM-bound), so bytes in flight set the speed
-    const uint4* wr = reinterpret_cast<const uint4*>(a.W + (int64_t)n * a.K);
-    for (int k0 = slot; k0 < nk; k0 += 4 * 32) {
-      uint4 wv[4];
+  for (int k0 = slot; k0 < nk; k0 += 4 * 32) {
+    if (k0 != slot) fetch(k0, cur);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int k = k0 + 32 * u;
-        wv[u] = k < nk ? __ldcs(wr + k) : make_uint4(0, 0, 0, 0);
-      }
+    for (int u = 0; u < 4; ++u) {
+      const int k = k0 + 32 * u;
+      if (!live || k >= nk) break;
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int k = k0 + 32 * u;
-        if (k >= nk) break;
-#pragma unroll
-        for (int i = 0; i < RB; ++i) {
-          const int r = r0 + i;
-          if (r < a.R) {
-            const uint4 xv = __ldg(reinterpret_cast<const uint4*>(a.A + (int64_t)r * a.K) + k);
-            acc[i] = dot16(wv[u], xv, acc[i]);
-          }
+      for (int i = 0; i < RB; ++i) {
+        const int r = r0 + i;
+        if (r < a.R) {
+          const uint4 xv = __ldg(reinterpret_cast<const uint4*>(a.A + (int64_t)r * a.K) + k);
+          acc[i] = dot16(cur[u], xv, acc[i]);
         }
       }
     }
