@@ -1,6 +1,6 @@
 """Tensor-parallel sharding of a quantized graph: qgraph dir -> one rank-local qgraph dir.
 
-The integer datapath splits exactly (SURVEY section 8e):
+The integer datapath splits exactly:
 
 * a linear whose input is replicated is split by output channels ("column parallel"):
   q / k / v by attention heads, gate / up by FFN channels, lm_head by vocabulary.  Its

@@ -114,7 +114,7 @@ def export_and_quantize(G, cfg_kwargs, seed, out_base: Path, name: str, fusions,
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("LLACCEL_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("LLACCEL_REFERENCE", str(Path(__file__).resolve().parents[3] / "reference")))
     args = ap.parse_args(argv)
     ref = Path(args.reference)
     G = load_reference(ref)
