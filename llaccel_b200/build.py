@@ -9,6 +9,7 @@ source file.
 from __future__ import annotations
 
 import argparse
+import fcntl
 import os
 import shutil
 import subprocess
@@ -50,11 +51,25 @@ def up_to_date() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compile if any source is newer than the library.  Processes that start together (one
+    per GPU rank) serialise on a lock file: the first rebuilds, the others find the library
+    up to date once they hold the lock."""
     if not force and up_to_date():
         return LIB
     LIBDIR.mkdir(exist_ok=True)
-    objdir = PKG / "_build"
-    objdir.mkdir(exist_ok=True)
+    with open(LIBDIR / ".build.lock", "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        try:
+            if not force and up_to_date():
+                return LIB
+            return _compile(verbose)
+        finally:
+            fcntl.flock(lock, fcntl.LOCK_UN)
+
+
+def _compile(verbose: bool) -> Path:
+    objdir = PKG / "_build" / str(os.getpid())
+    objdir.mkdir(parents=True, exist_ok=True)
     objs = []
     for src in sources():
         obj = objdir / (src.stem + ".o")
@@ -67,12 +82,13 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         if verbose and (r.stdout or r.stderr):
             print(r.stdout + r.stderr)
         objs.append(str(obj))
-    tmp = LIB.with_suffix(".so.tmp")
+    tmp = LIB.with_suffix(f".so.{os.getpid()}.tmp")
     cmd = [nvcc(), *ARCH_FLAGS, "-shared", "-o", str(tmp), *objs, "-lcuda", "-ldl"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
     os.replace(tmp, LIB)
+    shutil.rmtree(objdir, ignore_errors=True)
     return LIB
 
 
