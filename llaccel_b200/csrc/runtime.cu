@@ -1563,6 +1563,10 @@ static void session_create(llx_model* m, int batch, int max_rows, int keep, llx_
   LLX_CUDA(cudaMallocHost(&s->h_rec, sizeof(int32_t) * rows));
   LLX_CUDA(cudaMallocHost(&s->h_am, sizeof(int32_t) * rows));
   LLX_CUDA(cudaMallocHost(&s->h_pos, sizeof(int32_t) * 4));
+  // the clears above run on the legacy default stream, which the session's non-blocking
+  // stream does not wait for, and cudaMemset of device memory may return before it is
+  // done: finish them before any launch (or peer) can touch these buffers
+  LLX_CUDA(cudaDeviceSynchronize());
 }
 
 static void session_free(llx_session* s) {
