@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3] [--impl ours|reference]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N
 
-Workload (the data-parallel config quoted at 1/2/4/8 GPUs):
+Workload (config C3, the data-parallel config measured at 1/2/4/8 GPUs):
 Qwen2.5-0.5B architecture with random N(0, 0.02) weights and QKV bias, quantized int8
 per-channel; per GPU 128 independent sequences of 512 uniform-random prompt tokens, then
 greedy decode with the reference runtime's launch rule (255 decode launches: the 256th
@@ -238,9 +238,12 @@ def algorithmic_decode_bytes(m, prof: list[dict]) -> float:
 _SHORT_CPU_PROMPT = {"c4": 16, "c5": 16}
 
 
-def cpu_baseline(qdir: Path, prompt: np.ndarray, n_dec: int, gpu_hist: np.ndarray | None, config: str = "") -> dict:
+def cpu_baseline(qdir: Path, prompt: np.ndarray, n_dec: int, gpu_hist: np.ndarray | None, config: str = "",
+                 gpu_short=None) -> dict:
     """Oracle port on this host: prefill one sequence (untimed), then time n_dec decode
-    launches; compare the tokens with the GPU's decode history of the same sequence."""
+    launches; compare the tokens with the GPU's decode history of the same sequence.  For
+    the configs whose CPU sample prefills a short prompt, `gpu_short(prompt, n)` decodes
+    the same short prompt on the GPU (n decode launches) for the comparison."""
     import os as _os
     from oracle import golden_oracle as O
     cores = _os.cpu_count() or 1
@@ -248,7 +251,7 @@ def cpu_baseline(qdir: Path, prompt: np.ndarray, n_dec: int, gpu_hist: np.ndarra
     if config in _SHORT_CPU_PROMPT:
         prompt = prompt[: _SHORT_CPU_PROMPT[config]]
         n_dec = min(n_dec, 4)
-        gpu_hist = None  # other positions than the GPU run: no token comparison
+        gpu_hist = np.asarray(gpu_short([int(t) for t in prompt], n_dec)) if gpu_short else None
     toks = [int(t) for t in prompt]
     rows = o.prefill(toks)
     nxt = int(np.argmax(rows[-1][: o.vocab]))
@@ -539,7 +542,14 @@ def run_ours(args, dist: Dist) -> None:
 
     base = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        base = cpu_baseline(full, prompts[0], min(args.cpu_decode, n_dec), hist[:, 0], cfg.name)
+        from llaccel_b200.cuda_backend import CudaModel
+
+        def gpu_short(prompt, n):
+            # one sequence on the loaded weights (own session): n decode launches after the prompt
+            with CudaModel(qdir, batch=1, device=dev, max_rows=64, share=m.models[0]) as one:
+                return one.generate(prompt, n + 1)["generated"][1:]
+
+        base = cpu_baseline(full, prompts[0], min(args.cpu_decode, n_dec), hist[:, 0], cfg.name, gpu_short)
     line = {
         "metric": f"decode tokens/s (bit-exact int8), {cfg.name}",
         "value": value, "unit": "tokens/s", "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,

@@ -132,6 +132,10 @@ llx_status llx_read_activation(llx_session* s, const char* name, void* dst, size
 
 const char* llx_last_error(void);
 const char* llx_version(void);
+/* Compute capability the library's kernels were compiled for, as loaded on `device`
+ * (major * 10 + minor: 100 for sm_100a), from the CUDA runtime's function attributes.
+ * No counterpart in the reference (it has no GPU code); lets a host check the build. */
+llx_status llx_binary_version(int device, int* version);
 
 /* Tensor parallelism over NCCL (NVLink / NVSwitch).  A tensor-parallel group is `world`
  * processes, one per GPU, each loading its rank graph (written by llaccel_b200.tp.shard:
@@ -158,7 +162,8 @@ llx_status llx_tp_init(llx_model* m, const void* id, int rank, int world);
  * `vocab` channels, lowest index on ties).  Semantics are those of a qgraph linear with
  * epilogue none followed by the argmax of golden.py:376.  The per-row argmax keys use a
  * fixed file-scope device array of 4096 rows held by every GPU that loads the library until
- * exit: R > 4096 is rejected with LLX_ERR_RANGE.  The call is synchronous on `stream`
+ * exit: R > 4096 is rejected with LLX_ERR_RANGE, and so is K > 131056 (beyond it the int32
+ * sums of K products of int8 values could wrap).  The call is synchronous on `stream`
  * (a cudaStream_t, NULL = default stream).  Its first call on a device looks up that
  * array's device address and sets kernel attributes, so make it before any stream capture.
  * All calls share the array: calls that overlap on the GPU race. */

@@ -31,7 +31,8 @@ INT32_MAX, INT32_MIN = 2**31 - 1, -(2**31)
 
 
 # ---------------------------------------------------------------------------------------
-# Architectures (BASELINE configs C1..C5)
+# Architectures of the five benchmark configs C1..C5 (tiny Llama, SmolLM2-135M, Qwen2.5-0.5B,
+# Qwen3-0.6B, Llama-3-8B), random-initialised
 # ---------------------------------------------------------------------------------------
 @dataclass
 class ArchConfig:
@@ -74,7 +75,7 @@ CONFIGS = {
     "c5": ArchConfig("c5", 4096, 32, 32, 8, 128, 14336, 128256, 1280, 5e5, 1e-5),
 }
 
-# Workloads quoted with each config (BASELINE.json configs[0..4]).
+# Workload of each config: sequences per GPU, prompt tokens, greedy decode tokens.
 WORKLOADS = {
     "c1": {"batch": 1, "prompt": 16, "decode": 64},
     "c2": {"batch": 32, "prompt": 128, "decode": 128},

@@ -23,6 +23,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 #include "kernels.h"
@@ -301,7 +302,7 @@ __device__ __forceinline__ void epi_unit(const LinearArgs& a, const int32_t (&ac
 #pragma unroll
     for (int j = 0; j < UW; ++j) o[j] = silu_fast(o[j], Mi, a.silu_Si, a.silu_sh, s_sig);
   }
-  store_i16<UW>(reinterpret_cast<int16_t*>(dst) + (int64_t)r * ld + col, o);
+  if (dst) store_i16<UW>(reinterpret_cast<int16_t*>(dst) + (int64_t)r * ld + col, o);  // null: argmax only
   if (a.amax_key) {
 #pragma unroll
     for (int j = 0; j < UW; ++j) {
@@ -808,16 +809,18 @@ template <int NT, int S>
 static cudaError_t launch_tc_t(const CUtensorMap& ma, const CUtensorMap& mw, const LinearArgs& a, int ksplit,
                                int32_t* err, cudaStream_t st) {
   using L = tc::Smem<NT, S>;
-  static bool attr_set[64] = {};
+  // per-device "attributes set" flags: host threads may launch concurrently (sessions on
+  // several devices, the allocation-free entry point); setting an attribute twice is harmless
+  static std::atomic<bool> attr_set[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!attr_set[dev]) {
+  if (!attr_set[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(tc::k_linear_tc<NT, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(tc::k_linear_tc<NT, S>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
+    attr_set[dev].store(true, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((a.N + NT - 1) / NT, (a.R + tc::BM - 1) / tc::BM * ksplit, 1);
@@ -846,15 +849,15 @@ template <int NT, int S, int EW>
 static cudaError_t launch_tc_persistent_t(const CUtensorMap& ma, const CUtensorMap& mw, const LinearArgs& a,
                                           int grid, int32_t* err, cudaStream_t st) {
   using L = tc::Smem<NT, S>;
-  static bool attr_set[64] = {};
+  static std::atomic<bool> attr_set[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!attr_set[dev]) {
+  if (!attr_set[dev].load(std::memory_order_acquire)) {
     const cudaError_t e = cudaFuncSetAttribute(tc::k_linear_tc_persistent<NT, S, EW>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
     if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
+    attr_set[dev].store(true, std::memory_order_release);
   }
   const cudaError_t e = launch_k(tc::k_linear_tc_persistent<NT, S, EW>, dim3(grid), dim3(64 + 32 * EW), L::kBytes,
                                  st, ma, mw, a, err);

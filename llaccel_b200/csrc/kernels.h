@@ -76,7 +76,8 @@ struct LinearArgs {
   const int32_t* bias;  // [N] or null
   const int32_t* rq;    // [N][2] {M, S}
   const int16_t* aux;   // [R][N] i16 (RESADD / MUL) or null
-  void* out;            // [R][N] i16, or i8 when out_i8, or raw i32 sums when out_i32
+  void* out;            // [R][N] i16, or i8 when out_i8, or raw i32 sums when out_i32; null for an
+                        // i16 output with fused argmax: only the argmax keys are produced
   int R, N, K;
   int out_i8;
   int out_i32;          // tensor-parallel partial: store sum_k A*W as int32, no bias / requant

@@ -28,6 +28,9 @@ namespace llx {
 
 // Rows per call (one argmax key each), plus one slot for the pipeline error word.
 constexpr int kNoAllocMaxRows = 4096;
+// The int32 tensor-core accumulators are exact while K * 128 * 128 < 2^31: the largest K
+// (a multiple of 16) below 2^17.  Beyond it a sum could wrap and the argmax would be wrong.
+constexpr int kNoAllocMaxK = 131056;
 static __device__ __align__(256) unsigned long long g_noalloc_scratch[kNoAllocMaxRows + 1];
 
 extern int g_pdl;
@@ -82,6 +85,11 @@ extern "C" llx_status llx_linear_argmax_noalloc(const int8_t* A, const int8_t* W
     noalloc_set_error("llx_linear_argmax_noalloc: K must be a multiple of 16, N of 8, and 1 <= vocab <= N");
     return LLX_ERR_INVALID;
   }
+  if (K > kNoAllocMaxK) {
+    noalloc_set_error("llx_linear_argmax_noalloc: K = " + std::to_string(K) + " exceeds " +
+                      std::to_string(kNoAllocMaxK) + ", the largest K whose int32 sums cannot wrap");
+    return LLX_ERR_RANGE;
+  }
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(logits)) & 15) {
     noalloc_set_error("llx_linear_argmax_noalloc: A, W and logits must be 16-byte aligned");
     return LLX_ERR_INVALID;
@@ -115,9 +123,11 @@ extern "C" llx_status llx_linear_argmax_noalloc(const int8_t* A, const int8_t* W
     e = launch_linear_tc(map_a, map_w, a, nt, 1, fault, st);
   }
   if (e == cudaSuccess) e = launch_amax_finish(scratch, argmax, R, st);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  // the error word is read on the caller's stream (never the legacy default stream, which
+  // would wait for every other blocking stream of the device), then that stream is drained
   int32_t f = 0;
-  if (e == cudaSuccess) e = cudaMemcpy(&f, fault, sizeof(int32_t), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&f, fault, sizeof(int32_t), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) {
     noalloc_set_error(std::string("llx_linear_argmax_noalloc: ") + cudaGetErrorString(e));
     return e == cudaErrorMemoryAllocation ? LLX_ERR_OOM : LLX_ERR_CUDA;

@@ -877,10 +877,16 @@ struct llx_session {
   unsigned long long* d_amax_key = nullptr;  // [B*max_rows] fused argmax keys of the output linear
   int16_t* d_gather = nullptr;  // tensor parallelism: all-gathered logits shards [world][rows][vocab_padded]
   size_t gather_n = 0;
-  cudaGraphExec_t decode_exec = nullptr;
+  // decode-step graphs: [0] records only the argmax (the output linear stores no logits),
+  // [1] also stores the logits rows
+  cudaGraphExec_t decode_exec[2] = {nullptr, nullptr};
   int decode_launches = 0;
+  // the output linear stores its logits (cleared while a logits-free decode graph is captured
+  // or profiled; the fused argmax keys are produced either way)
+  bool store_logits = true;
   int last_R = 0, last_Rtail = 0;
   bool last_tail = false;
+  bool last_logits = true;  // the last launch stored its logits rows
 };
 
 namespace llx {
@@ -1066,6 +1072,8 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
           a.amax_key = s->d_amax_key;
           a.amax_vocab = local_vocab(m);
           a.amax_base = m->vocab_base;
+          // argmax-only launches skip the logits store: nothing reads them
+          if (!s->store_logits) a.out = nullptr;
         }
         if (path == 3)
           e = launch_gemm_tc(s, bd, x.in, a, false);
@@ -1436,6 +1444,7 @@ static void run_launch(llx_session* s, int M, int pos, bool with_embed, const in
   s->last_R = R;
   s->last_Rtail = Rtail;
   s->last_tail = tail;
+  s->last_logits = true;
 }
 
 // logits of the last launch's first `rows` output rows -> host [rows][vocab_padded_full].
@@ -1489,28 +1498,35 @@ static void stage_tokens(llx_session* s, const int32_t* tokens, int n) {
   LLX_CUDA(cudaMemcpyAsync(s->d_tokens, s->h_tok, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s->st));
 }
 
-static void build_decode_graph(llx_session* s) {
-  if (s->decode_exec) return;
+// The M = 1 decode step as a CUDA graph; with_logits selects the variant whose output
+// linear also stores the logits rows (otherwise only the fused argmax keys are produced).
+static cudaGraphExec_t build_decode_graph(llx_session* s, bool with_logits) {
+  cudaGraphExec_t& exec = s->decode_exec[with_logits ? 1 : 0];
+  if (exec) return exec;
   llx_model* m = s->m;
   Binding bd = bind(s, false);
   LLX_CUDA(cudaStreamSynchronize(s->st));
   cudaGraph_t graph;
   LLX_CUDA(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
   int n = 0;
+  s->store_logits = with_logits;
   try {
     n = enqueue_steps(s, bd, 0, m->steps.size(), s->B, 1);
     launch_output_argmax(s, bd.p[m->output_act], s->B);
     LLX_CUDA(launch_k(k_decode_finalize, dim3(1), dim3(256), 0, s->st, (const int32_t*)s->d_argmax, s->d_tokens,
                       s->d_hist, s->d_pos, s->d_step, s->B, s->hist_cap));
   } catch (...) {
+    s->store_logits = true;
     cudaStreamEndCapture(s->st, &graph);
     throw;
   }
+  s->store_logits = true;
   LLX_CUDA(cudaStreamEndCapture(s->st, &graph));
-  const cudaError_t e = cudaGraphInstantiate(&s->decode_exec, graph, 0);
+  const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
   cudaGraphDestroy(graph);
   LLX_CUDA(e);
   s->decode_launches = n + 2;
+  return exec;
 }
 
 static void session_create(llx_model* m, int batch, int max_rows, int keep, llx_session* s) {
@@ -1576,7 +1592,8 @@ static void session_free(llx_session* s) {
     s->m->n_sessions--;
   }
   if (s->st) cudaStreamSynchronize(s->st);
-  if (s->decode_exec) cudaGraphExecDestroy(s->decode_exec);
+  for (cudaGraphExec_t g : s->decode_exec)
+    if (g) cudaGraphExecDestroy(g);
   for (void* p : {(void*)s->arena, (void*)s->kv, (void*)s->d_tokens, (void*)s->d_rec, (void*)s->d_argmax,
                   (void*)s->d_hist, (void*)s->d_pos, (void*)s->d_amax_key, (void*)s->d_gather})
     if (p) cudaFree(p);
@@ -1618,6 +1635,16 @@ extern "C" {
 
 const char* llx_last_error(void) { return g_err.c_str(); }
 const char* llx_version(void) { return "llx 0.1 sm_100a"; }
+
+llx_status llx_binary_version(int device, int* version) {
+  return guarded([&] {
+    require(version != nullptr, LLX_ERR_INVALID, "null argument");
+    LLX_CUDA(cudaSetDevice(device));
+    cudaFuncAttributes fa{};
+    LLX_CUDA(cudaFuncGetAttributes(&fa, k_decode_finalize));
+    *version = fa.binaryVersion;
+  });
+}
 
 llx_status llx_model_load(const char* dir, const llx_opts* opts, llx_model** out) {
   return guarded([&] {
@@ -1748,11 +1775,12 @@ llx_status llx_run(llx_session* s, const int32_t* tokens, int M, int pos, const 
     stage_tokens(s, tokens, s->B * M);
     const bool identity = !rec_rows || n_rec == M;
     if (M == 1 && identity) {
-      build_decode_graph(s);
+      cudaGraphExec_t g = build_decode_graph(s, logits != nullptr);
       set_pos(s, pos);
-      LLX_CUDA(cudaGraphLaunch(s->decode_exec, s->st));
+      LLX_CUDA(cudaGraphLaunch(g, s->st));
       s->last_R = s->last_Rtail = s->B;
       s->last_tail = false;
+      s->last_logits = logits != nullptr;
     } else {
       run_launch(s, M, pos, true, rec_rows, n_rec);
     }
@@ -1842,12 +1870,13 @@ llx_status llx_generate(llx_session* s, const int32_t* prompts, int L, int n_tok
     if (n_tokens > 0)
       for (int b = 0; b < B; ++b) generated[(size_t)b * n_tokens] = nxt[b];
     if (n_dec > 0) {
-      build_decode_graph(s);
+      cudaGraphExec_t g = build_decode_graph(s, logits != nullptr);
+      s->last_logits = logits != nullptr;
       stage_tokens(s, nxt.data(), B);
       set_pos(s, L);
       if (logits) lg.resize((size_t)B * VP);
       for (int i = 0; i < n_dec; ++i) {
-        LLX_CUDA(cudaGraphLaunch(s->decode_exec, s->st));
+        LLX_CUDA(cudaGraphLaunch(g, s->st));
         if (logits) {
           fetch_logits(s, B, lg.data());
           for (int b = 0; b < B; ++b)
@@ -1883,9 +1912,10 @@ llx_status llx_decode_async(llx_session* s, int pos, int n_steps) {
     require(n_steps >= 0 && pos >= 0 && pos + n_steps <= s->m->max_seq, LLX_ERR_RANGE,
             "decode positions exceed max_seq");
     cudaSetDevice(s->m->device);
-    build_decode_graph(s);
+    cudaGraphExec_t g = build_decode_graph(s, false);
+    s->last_logits = false;
     set_pos(s, pos);
-    for (int i = 0; i < n_steps; ++i) LLX_CUDA(cudaGraphLaunch(s->decode_exec, s->st));
+    for (int i = 0; i < n_steps; ++i) LLX_CUDA(cudaGraphLaunch(g, s->st));
   });
 }
 
@@ -1910,9 +1940,9 @@ void* llx_session_stream(llx_session* s) { return s ? (void*)s->st : nullptr; }
 
 int llx_decode_launches_per_step(llx_session* s) {
   if (!s) return -1;
-  if (!s->decode_exec) {
+  if (!s->decode_exec[0]) {
     try {
-      build_decode_graph(s);
+      build_decode_graph(s, false);
     } catch (const std::exception& e) {
       g_err = e.what();
       return -1;
@@ -1955,8 +1985,10 @@ llx_status llx_profile_decode(llx_session* s, int pos, int iters, float* ms, dou
           case SK::RmsNorm: b = 2.0 * x.K + R * cols(x.in) * (x.out2 >= 0 ? 5.0 : 4.0); break;
           case SK::Quant: b = R * cols(x.in) * 3.0; break;
           case SK::Linear:
+            // the decode loop's output linear stores no logits (argmax keys only)
             b = (double)x.N * x.K + 8.0 * x.N + (x.bias_off >= 0 ? 4.0 * x.N : 0.0) + (double)R * x.K +
-                (double)R * x.N * (x.out_i8 ? 1 : 2) + (x.in2 >= 0 ? 2.0 * R * x.N : 0.0);
+                (x.out == m->output_act && output_argmax_fused(m, R) ? 0.0 : (double)R * x.N * (x.out_i8 ? 1 : 2)) +
+                (x.in2 >= 0 ? 2.0 * R * x.N : 0.0);
             o = 2.0 * R * x.N * x.K;
             break;
           case SK::Rope:
@@ -2008,14 +2040,22 @@ llx_status llx_profile_decode(llx_session* s, int pos, int iters, float* ms, dou
       // one untimed launch, then `iters` timed launches; a step folded into a neighbour
       // (it launches nothing at M = 1) reports zero time and zero bytes
       int launched = 1;
-      for (int it = 0; it <= iters; ++it) {
-        if (it == 1) LLX_CUDA(cudaEventRecord(e0, s->st));
-        if (i < (int)m->steps.size()) {
-          launched = enqueue_steps(s, bd, i, i + 1, R, 1);
-        } else {
-          launch_output_argmax(s, bd.p[m->output_act], R);
+      s->store_logits = false;  // as in the decode loop's graph
+      try {
+        for (int it = 0; it <= iters; ++it) {
+          if (it == 1) LLX_CUDA(cudaEventRecord(e0, s->st));
+          if (i < (int)m->steps.size()) {
+            launched = enqueue_steps(s, bd, i, i + 1, R, 1);
+          } else {
+            launch_output_argmax(s, bd.p[m->output_act], R);
+          }
         }
+      } catch (...) {
+        s->store_logits = true;
+        throw;
       }
+      s->store_logits = true;
+      s->last_logits = false;
       if (launched == 0) b = o = 0;
       LLX_CUDA(cudaEventRecord(e1, s->st));
       LLX_CUDA(cudaEventSynchronize(e1));
@@ -2055,6 +2095,8 @@ llx_status llx_read_activation(llx_session* s, const char* name, void* dst, size
     require(it != m->act_id.end(), LLX_ERR_INVALID, std::string("unknown activation ") + name);
     const int a = it->second;
     require(s->keep || a == m->output_act, LLX_ERR_INVALID, "activation buffers are reused; create the session with keep_acts=1");
+    require(a != m->output_act || s->last_logits, LLX_ERR_INVALID,
+            "the last launch recorded only the argmax (no logits were stored)");
     bool in_tail = false;
     for (size_t i = m->tail_start; i < m->steps.size(); ++i)
       for (int o : step_outs(m->steps[i]))

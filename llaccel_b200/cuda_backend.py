@@ -58,6 +58,7 @@ SIGNATURES = {
                                             C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
     "llx_last_error": (C.c_char_p, []),
     "llx_version": (C.c_char_p, []),
+    "llx_binary_version": (C.c_int, [C.c_int, C.c_void_p]),
     "llx_tp_unique_id": (C.c_int, [C.c_void_p]),
     "llx_tp_init": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int]),
 }

@@ -239,14 +239,16 @@ def _exact_product(a, b):
     return a @ b
 
 
-def exact_matmul(a, w):
-    """Integer A @ W.T, exact through float64 (see module docstring)."""
+def exact_matmul(a, w, w64=None):
+    """Integer A @ W.T, exact through float64 (see module docstring).  `w64`: W already
+    converted to float64 (a cache; the same values)."""
     a = np.asarray(a)
     w = np.asarray(w)
     amax = int(np.abs(a.astype(I64)).max(initial=0))
     if a.shape[1] * amax * 128 >= 1 << 53:
         return a.astype(I64) @ w.astype(I64).T
-    return (a.astype(np.float64) @ w.astype(np.float64).T).astype(I64)
+    wf = w64 if w64 is not None else w.astype(np.float64)
+    return (a.astype(np.float64) @ wf.T).astype(I64)
 
 
 # ---------------------------------------------------------------------------------------
@@ -295,7 +297,16 @@ class OracleModel:
         self.embed = self.q.tensors["embed"]
         self.rope_cos = self.q.tensors["rope_cos"]
         self.rope_sin = self.q.tensors["rope_sin"]
+        # float64 copies of the int8 weights, made on first use (exact: int8 values);
+        # saves re-converting large matrices (the vocabulary projection) every launch
+        self._w64: dict[str, np.ndarray] = {}
         self.reset()
+
+    def _weights64(self, name: str) -> np.ndarray:
+        w = self._w64.get(name)
+        if w is None:
+            w = self._w64[name] = self.q.tensors[name].astype(np.float64)
+        return w
 
     def reset(self) -> None:
         """Zero the per-layer KV caches [Hkv][max_seq][D] (golden.py:266-272)."""
@@ -312,7 +323,7 @@ class OracleModel:
         N, K = int(op["N"]), int(op["K"])
         if w.shape != (N, K) or a.shape[1] != K:
             raise ValueError(f"linear {op['out']}: shapes A{a.shape} W{w.shape} vs N={N} K={K}")
-        return self._requant(op, exact_matmul(a, w), act)
+        return self._requant(op, exact_matmul(a, w, self._weights64(op["w"])), act)
 
     def _requant(self, op, acc, act):
         """Bias (64-bit add), per-channel requant and epilogue of an int32 accumulator
@@ -376,7 +387,7 @@ class OracleModel:
             a, w = act[op["in"]], T[op["w"]]
             if w.shape != (int(op["N"]), int(op["K"])) or a.shape[1] != int(op["K"]):
                 raise ValueError(f"linear_partial {op['out']}: shape mismatch")
-            acc = exact_matmul(a, w)
+            acc = exact_matmul(a, w, self._weights64(op["w"]))
             if np.abs(acc).max(initial=0) >= 2**31:
                 raise ValueError("int32 partial accumulator overflow")
             act[op["out"]] = acc

@@ -277,3 +277,13 @@ def test_long_context_batch_decode_matches_oracle(tmp_path, D, H, Hkv, S):
         for b in range(B):
             assert first[b] == want[b % 4], b
         assert m.generate_batch(prompts, n, prefill_rows=256) == first
+
+
+def test_kernels_are_sm100_binaries():
+    """What the CUDA runtime loaded from the library is sm_100 machine code (no JIT of PTX)."""
+    import ctypes as C
+    from llaccel_b200.cuda_backend import _check, load_library
+    lib = load_library()
+    v = C.c_int(0)
+    _check(lib, lib.llx_binary_version(0, C.byref(v)))
+    assert v.value == 100
