@@ -52,7 +52,8 @@ typedef struct llx_session llx_session;
 typedef struct {
   int device;    /* CUDA device ordinal */
   int fuse;      /* 1: fuse QUANT/KV_WRITE into their producers (default); 0: one kernel per op */
-  int gemm_path; /* 0 auto, 1 CUDA-core GEMV, 2 CUDA-core tiled, 3 tensor-core tcgen05 */
+  int gemm_path; /* 0 auto, 1 CUDA-core GEMV, 2 CUDA-core tiled, 3 tensor-core tcgen05, 4 tensor-core without
+                    the swapped-operand decode kernel (a cross-check of 3) */
   int pdl;       /* 1: programmatic dependent launch between the kernels of a launch (default) */
 } llx_opts;
 

@@ -127,6 +127,12 @@ cudaError_t launch_linear(const LinearArgs& a, int path, cudaStream_t st);
 // {16, 32, 64, 128, 256}; ksplit CTAs per cluster split K (1 = none).  err receives a
 // nonzero code if a pipeline wait timed out.
 cudaError_t make_tmap_i8(CUtensorMap* map, const void* base, int64_t rows, int64_t K, int box_rows);
+// Decode GEMM with swapped operands (gemm_sab.cu), R <= 128 rows: map_a with an nb-row box
+// (nb = sab_rows_per_tile(R)), map_w with a 128-row box; ksplit (1..16) CTAs per cluster
+// split K.  Same arguments and results as launch_linear_tc.
+int sab_rows_per_tile(int R);
+cudaError_t launch_linear_sab(const CUtensorMap& map_a, const CUtensorMap& map_w, const LinearArgs& a, int nb,
+                              int ksplit, int32_t* err, cudaStream_t st);
 cudaError_t prepare_linear_tc();
 cudaError_t launch_linear_tc(const CUtensorMap& map_a, const CUtensorMap& map_w, const LinearArgs& a, int nt,
                              int ksplit, int32_t* err, cudaStream_t st);

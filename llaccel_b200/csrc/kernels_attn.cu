@@ -42,9 +42,9 @@ __device__ __forceinline__ T block_reduce(T v, T* scratch, Op op) {
   return r;
 }
 
-__global__ void k_attention(const int8_t* __restrict__ q, const int8_t* __restrict__ kc, const int8_t* __restrict__ vc,
-                            int8_t* __restrict__ out, int M, int H, int Hkv, int D, int max_seq,
-                            const int* __restrict__ d_pos, int64_t Ms, int Ss, int64_t Mo, int So, int prob_bits,
+__global__ void k_attention(const int8_t* q, const int8_t* kc, const int8_t* vc,
+                            int8_t* out, int M, int H, int Hkv, int D, int max_seq,
+                            const int* d_pos, int64_t Ms, int Ss, int64_t Mo, int So, int prob_bits,
                             const uint16_t* __restrict__ luts) {
   pdl_trigger();
   pdl_wait();
@@ -183,9 +183,16 @@ static int dec_rb(int rep) {
 }
 
 
-// largest dynamic shared memory any decode launch of this geometry uses (cluster size 2)
+// one CTA per unit (cluster size 1) holds the scores of the whole context: allowed while its
+// shared memory fits the per-CTA limit
+constexpr size_t kDecSmemLimit = 227 * 1024;
+static bool dec_c1_fits(int RB, int D, int max_seq) { return dec_smem_bytes(RB, D, max_seq, 1) <= kDecSmemLimit; }
+
+// largest dynamic shared memory any decode launch of this geometry uses (cluster size 1 when
+// it fits, else 2)
 size_t attention_decode_smem_bytes(int H, int Hkv, int D, int max_seq) {
-  return dec_smem_bytes(dec_rb(H / Hkv), D, max_seq, 2);
+  const int RB = dec_rb(H / Hkv);
+  return dec_c1_fits(RB, D, max_seq) ? dec_smem_bytes(RB, D, max_seq, 1) : dec_smem_bytes(RB, D, max_seq, 2);
 }
 
 __device__ __forceinline__ int dot16_i8(const uint4& a, const uint4& b, int acc) {
@@ -286,8 +293,8 @@ __device__ __forceinline__ void dec_transpose4(uint32_t x0, uint32_t x1, uint32_
 
 template <int LPK, int RB>
 __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
-    const int8_t* __restrict__ q, const int8_t* __restrict__ kc, const int8_t* __restrict__ vc, int8_t* __restrict__ out,
-    int H, int Hkv, int max_seq, const int* __restrict__ d_pos, int64_t Ms, int Ss, int64_t Mo, int So, int prob_bits,
+    const int8_t* q, const int8_t* kc, const int8_t* vc, int8_t* out,
+    int H, int Hkv, int max_seq, const int* d_pos, int64_t Ms, int Ss, int64_t Mo, int So, int prob_bits,
     const uint16_t* __restrict__ luts, int32_t* err, int C, const AttnArgs rope) {
   constexpr int D = LPK * 16;
   constexpr int TK = dec_tile_keys(D);
@@ -866,7 +873,8 @@ static std::map<std::tuple<int, int, int, int>, int> g_occ;
 
 template <int LPK, int RB>
 static cudaError_t measure_dec_occupancy(int max_seq) {
-  for (int C = 2; C <= 8; C *= 2) {
+  for (int C = 1; C <= 8; C *= 2) {
+    if (C == 1 && !dec_c1_fits(RB, LPK * 16, max_seq)) continue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(C * 148, 1, 1);
     cfg.blockDim = dim3(kDecThreads);
@@ -888,11 +896,13 @@ static cudaError_t measure_dec_occupancy(int max_seq) {
 }
 
 // Cluster size: the largest C in {8, 4, 2} whose B * Hkv * groups clusters are all resident
-// at once (one wave: the slowest slice bounds the launch); 2 when no size fits in one wave.
+// at once (one wave: the slowest slice bounds the launch).  When no split fits in one wave
+// but one CTA per unit does, C = 1: every max / sum / output exchange is then a CTA barrier
+// instead of a cluster round trip.  Otherwise 2, and the hardware schedules the waves.
 template <int LPK, int RB>
 static int dec_cluster_size(int units, int max_seq) {
   std::lock_guard<std::mutex> lock(g_occ_mu);
-  for (int C = 8; C >= 2; C /= 2) {
+  for (int C = 8; C >= 1; C /= 2) {
     auto it = g_occ.find(std::make_tuple(LPK, RB, max_seq, C));
     if (it != g_occ.end() && it->second >= units) return C;
   }
@@ -1021,8 +1031,8 @@ __device__ __forceinline__ void pf_mma(int32_t (&d)[4], const uint32_t (&a)[4], 
 
 template <int D, bool FAST>
 __global__ void __launch_bounds__(kPfThreads) k_attention_prefill(
-    const int8_t* __restrict__ q, const int8_t* __restrict__ kc, const int8_t* __restrict__ vc, int8_t* __restrict__ out,
-    int M, int H, int Hkv, int max_seq, const int* __restrict__ d_pos, int64_t Ms, int Ss, int64_t Mo, int So,
+    const int8_t* q, const int8_t* kc, const int8_t* vc, int8_t* out,
+    int M, int H, int Hkv, int max_seq, const int* d_pos, int64_t Ms, int Ss, int64_t Mo, int So,
     int prob_bits, const uint16_t* __restrict__ luts) {
   using L = PfSmem<D>;
   constexpr int KB = D / 32;  // k-blocks of Q K^T

@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(256) k_gemv(LinearArgs a) {
       for (int i = 0; i < RB; ++i) {
         const int r = r0 + i;
         if (r < a.R) {
-          const uint4 xv = __ldg(reinterpret_cast<const uint4*>(a.A + (int64_t)r * a.K) + k);
+          const uint4 xv = reinterpret_cast<const uint4*>(a.A + (int64_t)r * a.K)[k];  // written by the previous kernel: coherent load
           acc[i] = dot16(cur[u], xv, acc[i]);
         }
       }
@@ -135,7 +135,7 @@ __global__ void __launch_bounds__(256) k_gemm_tiled(LinearArgs a) {
   for (int k0 = 0; k0 < a.K; k0 += TK) {
     const int kc = k0 + lch * 16;
     uint4 av = make_uint4(0, 0, 0, 0), wv = make_uint4(0, 0, 0, 0);
-    if (r0 + lrow < a.R && kc < a.K) av = __ldg(reinterpret_cast<const uint4*>(a.A + (int64_t)(r0 + lrow) * a.K + kc));
+    if (r0 + lrow < a.R && kc < a.K) av = *reinterpret_cast<const uint4*>(a.A + (int64_t)(r0 + lrow) * a.K + kc);
     if (n0 + lrow < a.N && kc < a.K) wv = __ldg(reinterpret_cast<const uint4*>(a.W + (int64_t)(n0 + lrow) * a.K + kc));
     __syncthreads();
     As[lrow][lch * 4 + 0] = av.x;

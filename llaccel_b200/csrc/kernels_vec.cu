@@ -19,9 +19,9 @@ int g_pdl = 1;
 static inline unsigned grid1d(int64_t n, int per_block) { return (unsigned)((n + per_block - 1) / per_block); }
 
 // ---- embedding gather (golden.py:369-373; host.cpp:108-113) ------------------------------
-__global__ void k_embed(const int32_t* __restrict__ tokens, const int16_t* __restrict__ embed,
-                        int16_t* __restrict__ out, int R, int dim, int vocab_rows, int32_t* err,
-                        unsigned long long* __restrict__ amax_key) {
+__global__ void k_embed(const int32_t* tokens, const int16_t* __restrict__ embed,
+                        int16_t* out, int R, int dim, int vocab_rows, int32_t* err,
+                        unsigned long long* amax_key) {
   pdl_trigger();
   pdl_wait();
   const int r = blockIdx.x;
@@ -46,7 +46,7 @@ cudaError_t launch_embed(const int32_t* tokens, const int16_t* embed, int16_t* o
   return cudaGetLastError();
 }
 
-__global__ void k_amax_finish(const unsigned long long* __restrict__ keys, int32_t* __restrict__ out, int R) {
+__global__ void k_amax_finish(const unsigned long long* keys, int32_t* out, int R) {
   pdl_trigger();
   pdl_wait();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
@@ -86,120 +86,143 @@ __device__ __forceinline__ uint2 pack8_i8(const int32_t* v) {
   return r;
 }
 
-__global__ void k_rmsnorm(const int16_t* __restrict__ x, const int16_t* __restrict__ gamma, int16_t* __restrict__ y,
-                          int8_t* __restrict__ y8, int nrows, int K, int64_t eps_t, int64_t C, int sh_post,
-                          int64_t Mq, int Sq) {
-  pdl_trigger();
-  pdl_wait();
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= nrows) return;
-  const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)warp * K);
-  const uint4* gr = reinterpret_cast<const uint4*>(gamma);
-  const int chunks = K / 8;
-  uint64_t ss = 0;
-  for (int c = lane; c < chunks; c += 32) {
-    int32_t v[8];
-    unpack8(xr[c], v);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) ss += (uint64_t)((int64_t)v[i] * v[i]);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  // every lane holds the full sum; the serial isqrt/udiv is cheap enough to replicate
-  // ss + eps_t < 2^48 (K <= 65536 values of |x| <= 2^15, eps_t < 2^32) and C < 2^40
-  const uint64_t tt = ss + (uint64_t)eps_t;
-  const uint32_t r = isqrt48_fast(tt);
-  uint64_t inv = udiv_fast((uint64_t)C, r > 1 ? r : 1);
-  if (inv > 65535) inv = 65535;
-  uint4* yr = reinterpret_cast<uint4*>(y + (int64_t)warp * K);
-  uint2* yq = y8 ? reinterpret_cast<uint2*>(y8 + (int64_t)warp * K) : nullptr;
-  for (int c = lane; c < chunks; c += 32) {
+// The row is read into registers for the sum of squares: every 16-byte load of the row is
+// issued before any is used.  The elementwise pass then re-reads the row's chunks (L1 hits)
+// in a rolled loop: a kernel in the decode chain runs each instruction about once, so a
+// short loop body fetched once beats unrolled straight-line code.
+//   ss = sum x^2 (u64), r = isqrt48(ss + eps_t), inv = min(65535, C / max(r, 1)),
+//   y = sat16(rshr(x * g * inv, sh_post)), y8 = sat8(mulshift(y, Mq, Sq))
+// y (i16) is stored only when a later step reads it.  fastq: Sq >= 32 and Mq < 2^31, so the
+// quant runs on the product's high word (mulshift_hi32).
+__device__ __noinline__ void rms_finish(const uint4* xr, const uint4* __restrict__ gr, int c0, int cstep,
+                                        int chunks, uint32_t inv, int sh_post, int64_t Mq, int Sq, bool fastq,
+                                        uint4* yr, uint2* yq) {
+#pragma unroll 1
+  for (int c = c0; c < chunks; c += cstep) {
     int32_t v[8], g[8], o[8];
     unpack8(xr[c], v);
-    unpack8(gr[c], g);
+    unpack8(__ldg(gr + c), g);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int64_t xg = (int64_t)v[i] * g[i];
-      o[i] = (int32_t)sat16(rshr(xg * (int64_t)inv, sh_post));
-    }
-    yr[c] = pack8(o);
+    for (int e = 0; e < 8; ++e) o[e] = (int32_t)sat16(rshr((int64_t)(v[e] * g[e]) * (int64_t)inv, sh_post));
+    if (yr) yr[c] = pack8(o);
     if (yq) {
       int32_t q[8];
+      if (fastq) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) q[i] = (int32_t)sat8(mulshift(o[i], Mq, Sq));
+        for (int e = 0; e < 8; ++e) q[e] = (int32_t)sat8(mulshift_hi32(o[e], (int32_t)Mq, Sq));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q[e] = (int32_t)sat8(mulshift(o[e], Mq, Sq));
+      }
       yq[c] = pack8_i8(q);
     }
   }
 }
 
-// Wide rows (K >= 2048, e.g. Llama-3-8B's 4096): one 256-thread block per row, so a small
-// batch still spreads its rows' sums over many SMs.  Same arithmetic as k_rmsnorm.
-__global__ void k_rmsnorm_wide(const int16_t* __restrict__ x, const int16_t* __restrict__ gamma,
-                               int16_t* __restrict__ y, int8_t* __restrict__ y8, int K, int64_t eps_t, int64_t C,
-                               int sh_post, int64_t Mq, int Sq) {
-  pdl_trigger();
-  pdl_wait();
-  __shared__ uint64_t part[8];
-  __shared__ uint32_t s_inv;
-  const int row = blockIdx.x, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)row * K);
-  const uint4* gr = reinterpret_cast<const uint4*>(gamma);
-  const int chunks = K / 8;
-  uint64_t ss = 0;
-  for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
-    int32_t v[8];
-    unpack8(xr[c], v);
+__device__ __forceinline__ uint64_t sumsq8(const uint4& x) {
+  int32_t v[8];
+  unpack8(x, v);
+  uint64_t s = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) ss += (uint64_t)((int64_t)v[i] * v[i]);
-  }
+  for (int e = 0; e < 8; ++e) s += (uint32_t)(v[e] * v[e]);
+  return s;
+}
+
+// one warp per row (K < 2048): CPL chunks of 8 values per lane
+template <int CPL>
+__global__ void __launch_bounds__(64) k_rmsnorm(const int16_t* x, const int16_t* __restrict__ gamma,
+                                                int16_t* y, int8_t* y8, int nrows, int K,
+                                                int64_t eps_t, int64_t C, int sh_post, int64_t Mq, int Sq, int fastq) {
+  pdl_trigger();
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int chunks = K / 8;
+  const uint4* gr = reinterpret_cast<const uint4*>(gamma);
+  uint4 xv[CPL];
+  // gamma is a model constant: bring this lane's chunks into L1 before the dependency wait
+#pragma unroll
+  for (int i = 0; i < CPL; ++i)
+    if (lane + 32 * i < chunks) asm volatile("prefetch.global.L1 [%0];" ::"l"(gr + lane + 32 * i));
+  pdl_wait();
+  if (row >= nrows) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)row * K);
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) xv[i] = lane + 32 * i < chunks ? xr[lane + 32 * i] : make_uint4(0, 0, 0, 0);
+  uint64_t ss = 0;
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) ss += sumsq8(xv[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  // ss + eps_t < 2^48 (K <= 65536 values of |x| <= 2^15, eps_t < 2^32) and C < 2^40
+  const uint32_t r = isqrt48_fast(ss + (uint64_t)eps_t);
+  uint64_t inv = udiv_fast((uint64_t)C, r > 1 ? r : 1);
+  if (inv > 65535) inv = 65535;
+  rms_finish(xr, gr, lane, 32, chunks, (uint32_t)inv, sh_post, Mq, Sq, fastq != 0,
+             y ? reinterpret_cast<uint4*>(y + (int64_t)row * K) : nullptr,
+             y8 ? reinterpret_cast<uint2*>(y8 + (int64_t)row * K) : nullptr);
+}
+
+// Wide rows (K >= 2048, e.g. Llama-3-8B's 4096): one 256-thread block per row, CPT chunks per
+// thread, so a small batch still spreads its rows over many SMs.  Same arithmetic.
+template <int CPT>
+__global__ void __launch_bounds__(256) k_rmsnorm_wide(const int16_t* x, const int16_t* __restrict__ gamma,
+                                                      int16_t* y, int8_t* y8, int K,
+                                                      int64_t eps_t, int64_t C, int sh_post, int64_t Mq, int Sq,
+                                                      int fastq) {
+  pdl_trigger();
+  __shared__ uint64_t part[8];
+  const int row = blockIdx.x, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int chunks = K / 8;
+  const uint4* gr = reinterpret_cast<const uint4*>(gamma);
+  uint4 xv[CPT];
+#pragma unroll
+  for (int i = 0; i < CPT; ++i)
+    if ((int)threadIdx.x + 256 * i < chunks) asm volatile("prefetch.global.L1 [%0];" ::"l"(gr + threadIdx.x + 256 * i));
+  pdl_wait();
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)row * K);
+#pragma unroll
+  for (int i = 0; i < CPT; ++i)
+    xv[i] = (int)threadIdx.x + 256 * i < chunks ? xr[threadIdx.x + 256 * i] : make_uint4(0, 0, 0, 0);
+  uint64_t ss = 0;
+#pragma unroll
+  for (int i = 0; i < CPT; ++i) ss += sumsq8(xv[i]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if (lane == 0) part[w] = ss;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    uint64_t t = 0;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += part[i];
-    const uint32_t r = isqrt48_fast(t + (uint64_t)eps_t);
-    uint64_t inv = udiv_fast((uint64_t)C, r > 1 ? r : 1);
-    s_inv = (uint32_t)(inv > 65535 ? 65535 : inv);
-  }
-  __syncthreads();
-  const int64_t inv = s_inv;
-  uint4* yr = reinterpret_cast<uint4*>(y + (int64_t)row * K);
-  uint2* yq = y8 ? reinterpret_cast<uint2*>(y8 + (int64_t)row * K) : nullptr;
-  for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
-    int32_t v[8], g[8], o[8];
-    unpack8(xr[c], v);
-    unpack8(gr[c], g);
+  uint64_t t = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] = (int32_t)sat16(rshr((int64_t)v[i] * g[i] * inv, sh_post));
-    yr[c] = pack8(o);
-    if (yq) {
-      int32_t q[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) q[i] = (int32_t)sat8(mulshift(o[i], Mq, Sq));
-      yq[c] = pack8_i8(q);
-    }
-  }
+  for (int i = 0; i < 8; ++i) t += part[i];
+  const uint32_t r = isqrt48_fast(t + (uint64_t)eps_t);
+  uint64_t inv = udiv_fast((uint64_t)C, r > 1 ? r : 1);
+  if (inv > 65535) inv = 65535;
+  rms_finish(xr, gr, threadIdx.x, 256, chunks, (uint32_t)inv, sh_post, Mq, Sq, fastq != 0,
+             y ? reinterpret_cast<uint4*>(y + (int64_t)row * K) : nullptr,
+             y8 ? reinterpret_cast<uint2*>(y8 + (int64_t)row * K) : nullptr);
 }
 
 cudaError_t launch_rmsnorm(const int16_t* x, const int16_t* gamma, int16_t* y, int8_t* y8, int nrows, int K,
                            int64_t eps_t, int64_t C, int sh_post, int64_t Mq, int Sq, cudaStream_t st) {
   if (nrows <= 0) return cudaSuccess;
+  const int fastq = (Sq >= 32 && Mq >= 0 && Mq < (int64_t)1 << 31) ? 1 : 0;
+  const int chunks = K / 8;
+  cudaError_t e;
   if (K >= 2048) {
-    const cudaError_t e = launch_k(k_rmsnorm_wide, dim3(nrows), dim3(256), 0, st, x, gamma, y, y8, K, eps_t, C,
-                                   sh_post, Mq, Sq);
-    return e != cudaSuccess ? e : cudaGetLastError();
+    const int cpt = (chunks + 255) / 256;
+    auto kern = cpt <= 1 ? k_rmsnorm_wide<1> : cpt <= 2 ? k_rmsnorm_wide<2> : cpt <= 4 ? k_rmsnorm_wide<4> : k_rmsnorm_wide<8>;
+    if (cpt > 8) return cudaErrorInvalidValue;
+    e = launch_k(kern, dim3(nrows), dim3(256), 0, st, x, gamma, y, y8, K, eps_t, C, sh_post, Mq, Sq, fastq);
+  } else {
+    const int cpl = (chunks + 31) / 32;
+    auto kern = cpl <= 1 ? k_rmsnorm<1> : cpl <= 2 ? k_rmsnorm<2> : cpl <= 4 ? k_rmsnorm<4> : k_rmsnorm<8>;
+    e = launch_k(kern, dim3(grid1d(nrows, 2)), dim3(64), 0, st, x, gamma, y, y8, nrows, K, eps_t, C, sh_post, Mq, Sq,
+                 fastq);
   }
-  const int warps_per_block = 4;
-  { const cudaError_t e_ = launch_k(k_rmsnorm, dim3(grid1d(nrows, warps_per_block)), dim3(32 * warps_per_block), 0, st, x, gamma, y, y8, nrows, K, eps_t, C,
-                                                                             sh_post, Mq, Sq); if (e_ != cudaSuccess) return e_; }
-  return cudaGetLastError();
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 // ---- QUANT i16 -> i8 (numerics.h:56) -------------------------------------------------------
-__global__ void k_quant(const int16_t* __restrict__ x, int8_t* __restrict__ y, int64_t n8, int64_t M, int S) {
+__global__ void k_quant(const int16_t* x, int8_t* y, int64_t n8, int64_t M, int S) {
   pdl_trigger();
   pdl_wait();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -220,10 +243,10 @@ cudaError_t launch_quant(const int16_t* x, int8_t* y, int64_t n, int64_t M, int 
 
 // ---- RoPE (numerics.h:75-84; NUMERICS.md:113-125) [+ QUANT] [+ K cache write] ------------
 // thread per (row, head, i < D/2): rotates the (i, i + D/2) pair.
-__global__ void k_rope(const int16_t* __restrict__ x, int16_t* __restrict__ y16, int8_t* __restrict__ y8,
-                       int64_t Mq, int Sq, int8_t* __restrict__ kcache, int R, int M, int H, int D,
+__global__ void k_rope(const int16_t* x, int16_t* y16, int8_t* y8,
+                       int64_t Mq, int Sq, int8_t* kcache, int R, int M, int H, int D,
                        const int16_t* __restrict__ cos_tab, const int16_t* __restrict__ sin_tab,
-                       const int* __restrict__ d_pos, int max_seq) {
+                       const int* d_pos, int max_seq) {
   pdl_trigger();
   pdl_wait();
   const int half = D >> 1;
@@ -293,9 +316,9 @@ __device__ __forceinline__ void rope_pair(const RopeJob& j, int r, int h, int i,
   }
 }
 
-__global__ void k_rope_group(RopeJob q, RopeJob k, const int8_t* __restrict__ v, int8_t* __restrict__ vcache,
+__global__ void k_rope_group(RopeJob q, RopeJob k, const int8_t* v, int8_t* vcache,
                              int Hkv, int R, int M, int D, const int16_t* __restrict__ cos_tab,
-                             const int16_t* __restrict__ sin_tab, const int* __restrict__ d_pos, int max_seq) {
+                             const int16_t* __restrict__ sin_tab, const int* d_pos, int max_seq) {
   pdl_trigger();
   pdl_wait();
   const int half = D >> 1;
@@ -337,8 +360,8 @@ cudaError_t launch_rope_group(const RopeJob& q, const RopeJob& k, const int8_t* 
 
 // ---- KV write (golden.py:344-351; funcsim.cpp:377-396) ----------------------------------
 // thread per 16-byte chunk of one (row, kv head) segment
-__global__ void k_kv_write(const int8_t* __restrict__ k, const int8_t* __restrict__ v, int8_t* __restrict__ kc,
-                           int8_t* __restrict__ vc, int R, int M, int Hkv, int D, const int* __restrict__ d_pos,
+__global__ void k_kv_write(const int8_t* k, const int8_t* v, int8_t* kc,
+                           int8_t* vc, int R, int M, int Hkv, int D, const int* d_pos,
                            int max_seq) {
   pdl_trigger();
   pdl_wait();
@@ -366,7 +389,7 @@ cudaError_t launch_kv_write(const int8_t* k, const int8_t* v, int8_t* kc, int8_t
 }
 
 // ---- elementwise ADD / MUL / SILU (numerics.h:45-55) ----------------------------------------
-__global__ void k_add(const int16_t* __restrict__ a, const int16_t* __restrict__ b, int16_t* __restrict__ y,
+__global__ void k_add(const int16_t* a, const int16_t* b, int16_t* y,
                       int64_t n8, int sh_b) {
   pdl_trigger();
   pdl_wait();
@@ -380,7 +403,7 @@ __global__ void k_add(const int16_t* __restrict__ a, const int16_t* __restrict__
   reinterpret_cast<uint4*>(y)[i] = pack8(o);
 }
 
-__global__ void k_mul(const int16_t* __restrict__ a, const int16_t* __restrict__ b, int16_t* __restrict__ y,
+__global__ void k_mul(const int16_t* a, const int16_t* b, int16_t* y,
                       int64_t n8, int sh) {
   pdl_trigger();
   pdl_wait();
@@ -394,7 +417,7 @@ __global__ void k_mul(const int16_t* __restrict__ a, const int16_t* __restrict__
   reinterpret_cast<uint4*>(y)[i] = pack8(o);
 }
 
-__global__ void k_silu(const int16_t* __restrict__ x, int16_t* __restrict__ y, int64_t n8, int64_t Mi, int Si,
+__global__ void k_silu(const int16_t* x, int16_t* y, int64_t n8, int64_t Mi, int Si,
                        int sh_out, const uint16_t* __restrict__ sig) {
   pdl_trigger();
   pdl_wait();
@@ -428,8 +451,8 @@ cudaError_t launch_silu(const int16_t* x, int16_t* y, int64_t n, int64_t Mi, int
 // Grid (rows, slices): each block takes one slice of a row's first `vocab` logits and folds
 // its best packed key (logit + 32768) << 32 | (0xFFFFFFFF - (base + n)) into keys[r] with a
 // 64-bit atomicMax (keys zeroed beforehand); the max key is the row's first maximum.
-__global__ void k_argmax(const int16_t* __restrict__ logits, int ld, int vocab, int base, int slice,
-                         unsigned long long* __restrict__ keys) {
+__global__ void k_argmax(const int16_t* logits, int ld, int vocab, int base, int slice,
+                         unsigned long long* keys) {
   pdl_trigger();
   pdl_wait();
   const int r = blockIdx.x;
@@ -474,7 +497,7 @@ cudaError_t launch_argmax(const int16_t* logits, int R, int ld, int vocab, int b
 // ---- tensor-parallel requant of all-reduced partial sums -----------------------------------
 // Eight channels per thread: one 32-byte load of accumulators, one 16-byte (i16) or 8-byte
 // (i8) store.  N is a multiple of 8, so a group never straddles two rows.
-__global__ void k_requant(const int32_t* __restrict__ acc, LinearArgs a) {
+__global__ void k_requant(const int32_t* acc, LinearArgs a) {
   pdl_trigger();
   pdl_wait();
   const int64_t groups = (int64_t)a.R * a.N / 8;
@@ -531,7 +554,7 @@ cudaError_t launch_requant(const int32_t* acc, const LinearArgs& a, cudaStream_t
 }
 
 // ---- row gather ----------------------------------------------------------------------------
-__global__ void k_gather_rows(const uint4* __restrict__ src, uint4* __restrict__ dst, const int32_t* __restrict__ idx,
+__global__ void k_gather_rows(const uint4* src, uint4* dst, const int32_t* idx,
                               int chunks) {
   pdl_trigger();
   pdl_wait();

@@ -34,6 +34,16 @@ __device__ __forceinline__ int64_t sat16(int64_t v) { return clampi(v, -32768, 3
 
 __device__ __forceinline__ int64_t mulshift(int64_t v, int64_t M, int S) { return rshr(mul64(v, M), S); }
 
+// mulshift of a 32-bit value for S >= 32 and 0 <= M < 2^31 from the 64-bit product's high
+// word: p = v * M, hi = floor(p / 2^32).  Then p >> S = hi >> (S - 32) and the rounding bit
+// (bit S - 1 of p) is bit S - 33 of hi, or for S = 32 the top bit of the low word.  Equal to
+// mulshift(v, M, S) for every int32 v.
+__device__ __forceinline__ int32_t mulshift_hi32(int32_t v, int32_t M, int S) {
+  const int32_t hi = __mulhi(v, M);
+  const uint32_t rbit = S >= 33 ? ((uint32_t)hi >> (S - 33)) & 1u : ((uint32_t)v * (uint32_t)M) >> 31;
+  return (hi >> (S - 32)) + (int32_t)rbit;
+}
+
 // floor(sqrt(t)) for t < 2^48, bit-serial (numerics.h:26-35): 24 iterations, one digit each.
 __device__ __forceinline__ uint32_t isqrt48(uint64_t t) {
   uint64_t rem = 0, root = 0;

@@ -814,7 +814,7 @@ static void load_model(llx_model* m, const std::string& dir) {
     LLX_CUDA(cudaMemcpy(m->d_luts, tab, sizeof(tab), cudaMemcpyHostToDevice));
   }
   LLX_CUDA(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, m->device));
-  if (m->opts.gemm_path == 0 || m->opts.gemm_path == 3) {
+  if (m->opts.gemm_path == 0 || m->opts.gemm_path >= 3) {
     int major = 0;
     LLX_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, m->device));
     require(major == 10, LLX_ERR_UNSUPPORTED, "the tensor-core path needs an sm_100 (B200) device");
@@ -966,6 +966,23 @@ static cudaError_t launch_gemm_tc(llx_session* s, const Binding& bd, int in, con
     ks = 1;
   }
   const int row_tiles = (R + 127) / 128;
+  // small decode batches (R <= 32): the swapped-operand kernel (128 channels x up to 32 rows
+  // per tile), K split over a cluster so that about one CTA per SM streams the weights.  Its
+  // split-K partial tile is [128][NB] int32, summed over DSMEM; above 32 rows that exchange
+  // costs more than the row-tile kernel's, which wins from 64 rows up (measured at C3).
+  if (R <= 32 && m->opts.gemm_path != 4) {
+    const int ch_tiles = (N + 127) / 128;
+    const int nkb = (K + 127) / 128;
+    int kss = (m->sms + ch_tiles / 2) / ch_tiles;
+    kss = std::max(1, std::min({kss, nkb, 8}));
+    const bool persistent = (N + 255) / 256 >= 2 * m->sms;
+    if (!persistent) {
+      const int nb = sab_rows_per_tile(R);
+      const CUtensorMap& mab = tmap(s, a.A, (int64_t)bd.rows[in], K, nb);
+      const CUtensorMap& mwb = tmap(s, a.W, N, K, 128);
+      return launch_linear_sab(mab, mwb, a, nb, kss, s->d_fault, s->st);
+    }
+  }
   const CUtensorMap& ma = tmap(s, a.A, (int64_t)bd.rows[in], K, 128);
   if (ks == 1) {
     for (int pnt : {256, 128}) {
@@ -985,9 +1002,11 @@ static int enqueue_steps(llx_session* s, const Binding& bd, size_t from, size_t 
   return launches;
 }
 
-// GEMM path of a linear step over R rows: 3 = tensor cores, else a CUDA-core schedule
+// GEMM path of a linear step over R rows: 3 = tensor cores (4: tensor cores without the
+// swapped-operand decode kernel, a cross-check), else a CUDA-core schedule
 static int gemm_path_for(const llx_model* m, int R) {
   int path = m->opts.gemm_path;
+  if (path == 4) return 3;
   if (path == 0) path = R >= 16 ? 3 : 1;
   return path;
 }
@@ -1042,8 +1061,8 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
                          m->vocab, s->d_err, s->d_amax_key, st);
         break;
       case SK::RmsNorm:
-        e = launch_rmsnorm((const int16_t*)P(x.in), (const int16_t*)dptr(m, x.gamma_off), (int16_t*)P(x.out),
-                           (int8_t*)P(x.out2), R * x.heads, x.K, x.eps_t, x.C, x.sh_post, x.Mq, x.Sq, st);
+        e = launch_rmsnorm((const int16_t*)P(x.in), (const int16_t*)dptr(m, x.gamma_off),
+                           (int16_t*)(x.out2 >= 0 ? Pused(x.out) : P(x.out)), (int8_t*)P(x.out2), R * x.heads, x.K, x.eps_t, x.C, x.sh_post, x.Mq, x.Sq, st);
         break;
       case SK::Quant:
         e = launch_quant((const int16_t*)P(x.in), (int8_t*)P(x.out), (int64_t)R * m->acts[x.in].cols, x.Mq, x.Sq, st);
@@ -1348,8 +1367,8 @@ static void plan_arena(llx_session* s) {
   s->arena_bytes = std::max<size_t>(extra, 256);
 }
 
-__global__ void k_decode_finalize(const int32_t* __restrict__ argmax, int32_t* __restrict__ tokens,
-                                  int32_t* __restrict__ hist, int32_t* pos, int32_t* step, int B, int cap) {
+__global__ void k_decode_finalize(const int32_t* argmax, int32_t* tokens,
+                                  int32_t* hist, int32_t* pos, int32_t* step, int B, int cap) {
   pdl_trigger();
   pdl_wait();
   __shared__ int s_step;

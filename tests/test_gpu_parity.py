@@ -52,7 +52,8 @@ def test_host_loop_activations_match_reference(name):
 
 
 @pytest.mark.parametrize("name", ["fx_v1", "c1_v2", "qwen3_tiny", "d128_tiny"])
-@pytest.mark.parametrize("fuse,gemm_path", [(False, 1), (False, 2), (False, 3), (True, 1), (True, 2), (True, 3)])
+@pytest.mark.parametrize("fuse,gemm_path", [(False, 1), (False, 2), (False, 3), (False, 4), (True, 1), (True, 2),
+                                             (True, 3), (True, 4)])
 def test_plan_and_gemm_variants_are_identical(name, fuse, gemm_path):
     rec, prompt, n = _rec(name)
     with CudaModel(GOLDEN / name, fuse=fuse, gemm_path=gemm_path) as m:
@@ -104,10 +105,12 @@ def test_stress_graphs_run_chunk_matches_oracle(tmp_path, cfg):
     (64, 48, "none", 0), (128, 256, "none", 0), (896, 1152, "none", 0), (576, 576, "resadd", 0),
     (256, 4864, "silu", 0), (512, 512, "mul", 0), (4864, 64, "none", 0), (14336, 32, "none", 0),
     (352, 2048, "none", 96), (1024, 40000, "none", 0), (160, 8, "none", 0)])
-@pytest.mark.parametrize("R", [16, 40, 128, 300])
+@pytest.mark.parametrize("R", [5, 16, 40, 128, 300])
 def test_linear_paths_match_oracle(tmp_path, K, N, epi, chain, R):
-    """Every GEMM schedule (GEMV, tiled dp4a, tcgen05 with and without cluster split-K) on
-    full-range int8 operands against the oracle, for all four epilogues and i8 outputs."""
+    """Every GEMM schedule (GEMV, tiled dp4a, tcgen05: the swapped-operand decode kernel for
+    R <= 128 (path 3), the row-tile kernel with and without cluster split-K (path 4, and
+    path 3 above 128 rows)) on full-range int8 operands against the oracle, for all four
+    epilogues and i8 outputs."""
     d = qgraph_synth.build_linear(tmp_path / "lin", K=K, N=N, epi=epi, chain_i8=chain, seed=K + N + R)
     o = O.OracleModel(d)
     rng = np.random.default_rng(R)
@@ -115,7 +118,7 @@ def test_linear_paths_match_oracle(tmp_path, K, N, epi, chain, R):
     rows[0] = 32767
     rows[1] = -32768
     want = o.run_chunk(rows, 0)
-    for path in (3, 1, 2):
+    for path in (3, 4, 1, 2):
         with CudaModel(d, max_rows=R, gemm_path=path) as m:
             np.testing.assert_array_equal(m.run_chunk(rows, 0), want, err_msg=f"path {path}")
 

@@ -34,7 +34,7 @@ def _build():
 
 
 @pytest.mark.parametrize("name", ["c1_v2", "qwen3_tiny", "d128_tiny"])
-@pytest.mark.parametrize("gemm_path", [0, 1, 3])
+@pytest.mark.parametrize("gemm_path", [0, 1, 3, 4])
 def test_tp1_rank_graph_matches_golden(tmp_path, name, gemm_path):
     _build()
     from llaccel_b200 import tp
