@@ -64,6 +64,18 @@ def parse_args():
 # ---------------------------------------------------------------------------------------
 # distributed plumbing
 # ---------------------------------------------------------------------------------------
+class _stdout_to_stderr:
+    """Redirect file descriptor 1 to 2 (C libraries included) for the duration."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        os.dup2(2, 1)
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
 class Dist:
     """One process per GPU (torchrun env): barrier and max-over-ranks timing.  backend
     "nccl" on GPUs; "gloo" serves the CPU tests of the same plumbing."""
@@ -84,8 +96,12 @@ class Dist:
             if backend == "nccl":
                 torch.cuda.set_device(self.local)
                 kw["device_id"] = torch.device("cuda", self.local)
-            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600), **kw)
-            self.pg = dist
+            # communicator set-up may print (e.g. NCCL's version line) on stdout, which must
+            # carry only the result line: send fd 1 to stderr meanwhile
+            with _stdout_to_stderr():
+                dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600), **kw)
+                self.pg = dist
+                self.barrier()
         if want != self.world and self.world > 1:
             raise SystemExit(f"--gpus {want} but WORLD_SIZE {self.world}")
 
@@ -413,7 +429,9 @@ def run_ours(args, dist: Dist) -> None:
     seq_groups = 1 if args.tp else dist.world  # independent sequence sets decoded per step
     # prefill launches of up to 512 rows per sequence, fewer when B*rows would exceed 64K rows
     max_rows = max(16, min(L, 512, (65536 // B) // 16 * 16))
-    m = CudaLanes(qdir, batch=B, lanes=lanes, device=dev, max_rows=max_rows, gemm_path=args.gemm_path, **model_kw)
+    with _stdout_to_stderr():  # a tensor-parallel model opens its NCCL communicator here
+        m = CudaLanes(qdir, batch=B, lanes=lanes, device=dev, max_rows=max_rows, gemm_path=args.gemm_path,
+                      **model_kw)
     t0 = time.perf_counter()
     recs = m.generate_batch(prompts.tolist(), 0, with_logits=False)  # prefill (untimed)
     prefill_s = time.perf_counter() - t0

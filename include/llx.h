@@ -116,8 +116,9 @@ void* llx_session_stream(llx_session* s);
 int llx_decode_launches_per_step(llx_session* s);
 
 /* Profiling. The plan's steps (one kernel each), and a per-step timing of the M=1 decode
- * plan at position pos: each step is launched alone `iters` times on the session stream
- * between CUDA events (every step is idempotent). Fills ms[i] (average per launch),
+ * plan at position pos: each step is launched alone `iters` times on the session stream,
+ * each launch between two CUDA events after a 256 MB write that evicts the L2 (every step
+ * is idempotent; the first 256 MB call allocates that buffer). Fills ms[i] (average per launch),
  * bytes[i] and ops[i] (algorithmic HBM bytes / integer ops of one launch) for up to n_max
  * steps plus the argmax kernel; *n_out = entries written. */
 int llx_plan_steps(const llx_model* m);

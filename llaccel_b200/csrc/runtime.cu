@@ -887,6 +887,7 @@ struct llx_session {
   int last_R = 0, last_Rtail = 0;
   bool last_tail = false;
   bool last_logits = true;  // the last launch stored its logits rows
+  uint8_t* d_flush = nullptr;  // profiling: a buffer twice the L2 size, written between timed launches
 };
 
 namespace llx {
@@ -1198,8 +1199,9 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
       }
       case SK::LinearGroup:
       case SK::Gated: {
-        if (gemm_path_for(m, R) != 3) {
-          // CUDA-core schedules run the constituent ops one by one
+        const int path = gemm_path_for(m, R);
+        if (path == 2) {
+          // the tiled CUDA-core schedule runs the constituent ops one by one
           int n = 0;
           for (const Step& p : x.parts) n += enqueue_one(s, bd, p, R, M);
           return n;
@@ -1238,7 +1240,8 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
             a.q_S = x.parts[2].Sq;
           }
         }
-        e = launch_gemm_tc(s, bd, x.in, a, x.kind == SK::Gated);
+        // tensor cores, or (few rows) the GEMV, which fuses the group / pair the same way
+        e = path == 3 ? launch_gemm_tc(s, bd, x.in, a, x.kind == SK::Gated) : launch_linear(a, 1, st);
         break;
       }
       case SK::RopeGroup: {
@@ -1614,7 +1617,7 @@ static void session_free(llx_session* s) {
   for (cudaGraphExec_t g : s->decode_exec)
     if (g) cudaGraphExecDestroy(g);
   for (void* p : {(void*)s->arena, (void*)s->kv, (void*)s->d_tokens, (void*)s->d_rec, (void*)s->d_argmax,
-                  (void*)s->d_hist, (void*)s->d_pos, (void*)s->d_amax_key, (void*)s->d_gather})
+                  (void*)s->d_hist, (void*)s->d_pos, (void*)s->d_amax_key, (void*)s->d_gather, (void*)s->d_flush})
     if (p) cudaFree(p);
   for (void* p : {(void*)s->h_tok, (void*)s->h_rec, (void*)s->h_am, (void*)s->h_pos, (void*)s->h_i16})
     if (p) cudaFreeHost(p);
@@ -1978,6 +1981,9 @@ const char* llx_step_label(const llx_model* m, int i) {
   return i == (int)m->steps.size() ? kArgmax : m->steps[i].label.c_str();
 }
 
+// the L2 flush of llx_profile_decode: twice the B200's 126 MB L2
+static constexpr size_t kFlushBytes = (size_t)256 << 20;
+
 llx_status llx_profile_decode(llx_session* s, int pos, int iters, float* ms, double* bytes, double* ops, int n_max,
                               int* n_out) {
   return guarded([&] {
@@ -1992,6 +1998,7 @@ llx_status llx_profile_decode(llx_session* s, int pos, int iters, float* ms, dou
     cudaEvent_t e0, e1;
     LLX_CUDA(cudaEventCreate(&e0));
     LLX_CUDA(cudaEventCreate(&e1));
+    if (!s->d_flush) LLX_CUDA(cudaMalloc(&s->d_flush, kFlushBytes));
     const int n = std::min<int>(n_max, (int)m->steps.size() + 1);
     const double T = pos + 1;
     for (int i = 0; i < n; ++i) {
@@ -2056,18 +2063,26 @@ llx_status llx_profile_decode(llx_session* s, int pos, int iters, float* ms, dou
       } else {
         b = output_argmax_fused(m, R) ? 12.0 * R : 2.0 * R * m->vocab_padded + 4.0 * R;
       }
-      // one untimed launch, then `iters` timed launches; a step folded into a neighbour
-      // (it launches nothing at M = 1) reports zero time and zero bytes
+      // one untimed launch, then `iters` timed launches, each alone between two events after
+      // a write of twice the L2 size (its inputs come from HBM, as in the decode chain); a
+      // step folded into a neighbour (it launches nothing at M = 1) reports zero time and bytes
       int launched = 1;
+      float total = 0.0f;
       s->store_logits = false;  // as in the decode loop's graph
       try {
         for (int it = 0; it <= iters; ++it) {
-          if (it == 1) LLX_CUDA(cudaEventRecord(e0, s->st));
+          LLX_CUDA(cudaMemsetAsync(s->d_flush, it & 1, kFlushBytes, s->st));
+          LLX_CUDA(cudaEventRecord(e0, s->st));
           if (i < (int)m->steps.size()) {
             launched = enqueue_steps(s, bd, i, i + 1, R, 1);
           } else {
             launch_output_argmax(s, bd.p[m->output_act], R);
           }
+          LLX_CUDA(cudaEventRecord(e1, s->st));
+          LLX_CUDA(cudaEventSynchronize(e1));
+          float t = 0;
+          LLX_CUDA(cudaEventElapsedTime(&t, e0, e1));
+          if (it > 0) total += t;
         }
       } catch (...) {
         s->store_logits = true;
@@ -2076,11 +2091,7 @@ llx_status llx_profile_decode(llx_session* s, int pos, int iters, float* ms, dou
       s->store_logits = true;
       s->last_logits = false;
       if (launched == 0) b = o = 0;
-      LLX_CUDA(cudaEventRecord(e1, s->st));
-      LLX_CUDA(cudaEventSynchronize(e1));
-      float t = 0;
-      LLX_CUDA(cudaEventElapsedTime(&t, e0, e1));
-      ms[i] = launched ? t / iters : 0.0f;
+      ms[i] = launched ? total / iters : 0.0f;
       bytes[i] = b;
       ops[i] = o;
     }
