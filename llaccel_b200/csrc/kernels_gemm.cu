@@ -52,55 +52,83 @@ __device__ __forceinline__ int dot16(const uint4& w, const uint4& x, int acc) {
   return acc;
 }
 
-// ---- GEMV: 8 output channels per 256-thread block, RB rows per block row -------------------
-// The weights are model constants: a thread's first four 16-byte weight loads are issued
-// before the grid dependency wait, so they stream while the previous kernel finishes.  Each
-// later round of four is requested together, before any of it is consumed.
+// ---- GEMV: CPB output channels per 256-thread block, RB rows per block row -----------------
+// Warp lanes split into CPB channels x LPC = 32 / CPB K slots; with 8 warps, K is cut into
+// 8 * LPC slots of 16-byte chunks.  The weights are model constants: the first round of
+// weight loads is issued before the grid dependency wait, so it streams while the previous
+// kernel finishes, and from then on the next round is always in flight while the current one
+// is consumed (two register buffers).  CPB = 4 (more blocks, half the serial rounds per
+// thread) serves long rows (K >= 8192, e.g. a down projection); CPB = 8 the others.
 // Fused forms (one launch instead of one per constituent linear):
 //   multi-output (a.nseg > 0): q/k/v over row-concatenated weights, each channel stored to
 //     its segment's output;
 //   GATED: the gate/up pair over the interleaved weights (rows 32j..32j+15 gate, 32j+16..
 //     32j+31 up of outputs 16j..16j+15): a thread accumulates the gate and the up row of its
 //     output, and the epilogue applies silu16(gate) * up, the shift and the quant.
-template <int RB, bool GATED>
+template <bool GATED>
+__device__ __forceinline__ void gemv_finish(const LinearArgs& a, int r, int oo, int32_t s0, int32_t s1) {
+  if (GATED) {
+    const int ng = 32 * (oo >> 4) + (oo & 15), nu = ng + 16;
+    const int64_t tg = sat16(mulshift((int64_t)s0 + (a.bias ? a.bias[ng] : 0), a.rq[2 * ng], a.rq[2 * ng + 1]));
+    const int64_t tu = sat16(mulshift((int64_t)s1 + (a.bias ? a.bias[nu] : 0), a.rq[2 * nu], a.rq[2 * nu + 1]));
+    const int64_t sg = silu16(tg, a.silu_Mi, a.silu_Si, a.silu_sh, a.luts + kLutSig);
+    const int64_t f = sat16(rshr(tu * sg, a.aux_shift));
+    const int64_t off = (int64_t)r * a.Nout + oo;
+    if (a.g_out) a.g_out[off] = (int16_t)sg;
+    if (a.f_out) a.f_out[off] = (int16_t)f;
+    if (a.q_out) a.q_out[off] = (int8_t)sat8(mulshift(f, a.q_M, a.q_S));
+  } else if (a.nseg > 0) {
+    // multi-output linear (epilogue none): the channel's segment and its output
+    int sgi = 0;
+    while (sgi + 1 < a.nseg && oo >= a.seg_start[sgi + 1]) ++sgi;
+    const int ld = a.seg_start[sgi + 1] - a.seg_start[sgi], col = oo - a.seg_start[sgi];
+    const int64_t v = mulshift((int64_t)s0 + (a.bias ? a.bias[oo] : 0), a.rq[2 * oo], a.rq[2 * oo + 1]);
+    if (a.seg_i8[sgi])
+      reinterpret_cast<int8_t*>(a.seg_out[sgi])[(int64_t)r * ld + col] = (int8_t)sat8(v);
+    else
+      reinterpret_cast<int16_t*>(a.seg_out[sgi])[(int64_t)r * ld + col] = (int16_t)sat16(v);
+  } else {
+    store_out(a, r, oo, linear_epilogue(s0, r, oo, a));
+  }
+}
+
+template <int RB, bool GATED, int CPB>
 __global__ void __launch_bounds__(256) k_gemv(LinearArgs a) {
   pdl_trigger();
-  constexpr int NW = GATED ? 2 : 1;  // weight rows per output channel
-  __shared__ int32_t part[8][NW][8][RB];  // [warp][row kind][channel][row]
+  constexpr int NW = GATED ? 2 : 1;        // weight rows per output channel
+  constexpr int U = GATED ? 2 : 4;         // 16-byte loads per row and round
+  constexpr int LPC = 32 / CPB;            // lanes per channel
+  constexpr int SLOTS = 8 * LPC;           // K slots of the block
+  __shared__ int32_t part[8][NW][CPB][RB];  // [warp][row kind][channel][row]
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c = lane >> 2, sub = lane & 3;
-  const int slot = w * 4 + sub;  // 0..31 over K
-  const int o0 = blockIdx.x * 8, r0 = blockIdx.y * RB;
+  const int c = lane / LPC, sub = lane % LPC;
+  const int slot = w * LPC + sub;
+  const int o0 = blockIdx.x * CPB, r0 = blockIdx.y * RB;
   const int o = o0 + c;
   const int nout = GATED ? a.Nout : a.N;
   const int nk = a.K >> 4;
   const bool live = o < nout;
   const int wrow = GATED ? 32 * (o >> 4) + (o & 15) : o;  // gate row (the up row is 16 further)
-  const uint4* wr[NW];
-  wr[0] = reinterpret_cast<const uint4*>(a.W + (int64_t)(live ? wrow : 0) * a.K);
-  if (GATED) wr[NW - 1] = wr[0] + (int64_t)16 * nk;
-  auto fetch = [&](int k0, uint4 (&wv)[NW][4]) {
+  const uint4* wr0 = reinterpret_cast<const uint4*>(a.W + (int64_t)(live ? wrow : 0) * a.K);
+  const uint4* wr1 = wr0 + (int64_t)16 * nk;
+  auto fetch = [&](int k0, uint4 (&wv)[NW][U]) {
 #pragma unroll
-    for (int h = 0; h < NW; ++h)
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int k = k0 + 32 * u;
-        wv[h][u] = live && k < nk ? __ldcs(wr[h] + k) : make_uint4(0, 0, 0, 0);
-      }
+    for (int u = 0; u < U; ++u) {
+      const int k = k0 + SLOTS * u;
+      const bool ok = live && k < nk;
+      wv[0][u] = ok ? __ldcs(wr0 + k) : make_uint4(0, 0, 0, 0);
+      if (GATED) wv[NW - 1][u] = ok ? __ldcs(wr1 + k) : make_uint4(0, 0, 0, 0);
+    }
   };
-  uint4 cur[NW][4];
-  fetch(slot, cur);
-  pdl_wait();  // the activation rows and the output buffers belong to earlier kernels
   int32_t acc[NW][RB];
 #pragma unroll
   for (int h = 0; h < NW; ++h)
 #pragma unroll
     for (int i = 0; i < RB; ++i) acc[h][i] = 0;
-  for (int k0 = slot; k0 < nk; k0 += 4 * 32) {
-    if (k0 != slot) fetch(k0, cur);
+  auto consume = [&](int k0, const uint4 (&wv)[NW][U]) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int k = k0 + 32 * u;
+    for (int u = 0; u < U; ++u) {
+      const int k = k0 + SLOTS * u;
       if (!live || k >= nk) break;
 #pragma unroll
       for (int i = 0; i < RB; ++i) {
@@ -109,18 +137,28 @@ __global__ void __launch_bounds__(256) k_gemv(LinearArgs a) {
           // written by the previous kernel: a coherent load
           const uint4 xv = reinterpret_cast<const uint4*>(a.A + (int64_t)r * a.K)[k];
 #pragma unroll
-          for (int h = 0; h < NW; ++h) acc[h][i] = dot16(cur[h][u], xv, acc[h][i]);
+          for (int h = 0; h < NW; ++h) acc[h][i] = dot16(wv[h][u], xv, acc[h][i]);
         }
       }
     }
+  };
+  constexpr int STEP = SLOTS * U;  // K chunks per round of the block
+  uint4 b0[NW][U], b1[NW][U];
+  fetch(slot, b0);
+  pdl_wait();  // the activation rows and the output buffers belong to earlier kernels
+  for (int k0 = slot; k0 < nk; k0 += 2 * STEP) {
+    fetch(k0 + STEP, b1);  // next round in flight while this one is consumed
+    consume(k0, b0);
+    if (k0 + STEP >= nk) break;
+    fetch(k0 + 2 * STEP, b0);
+    consume(k0 + STEP, b1);
   }
 #pragma unroll
   for (int h = 0; h < NW; ++h)
 #pragma unroll
-    for (int i = 0; i < RB; ++i) {
-      acc[h][i] += __shfl_xor_sync(0xffffffffu, acc[h][i], 1);
-      acc[h][i] += __shfl_xor_sync(0xffffffffu, acc[h][i], 2);
-    }
+    for (int i = 0; i < RB; ++i)
+#pragma unroll
+      for (int x = 1; x < LPC; x <<= 1) acc[h][i] += __shfl_xor_sync(0xffffffffu, acc[h][i], x);
   if (sub == 0) {
 #pragma unroll
     for (int h = 0; h < NW; ++h)
@@ -128,7 +166,7 @@ __global__ void __launch_bounds__(256) k_gemv(LinearArgs a) {
       for (int i = 0; i < RB; ++i) part[w][h][c][i] = acc[h][i];
   }
   __syncthreads();
-  for (int t = threadIdx.x; t < 8 * RB; t += blockDim.x) {
+  for (int t = threadIdx.x; t < CPB * RB; t += blockDim.x) {
     const int cc = t / RB, i = t % RB;
     const int oo = o0 + cc, r = r0 + i;
     if (oo >= nout || r >= a.R) continue;
@@ -139,31 +177,18 @@ __global__ void __launch_bounds__(256) k_gemv(LinearArgs a) {
 #pragma unroll
       for (int ww = 0; ww < 8; ++ww) sum[h] += part[ww][h][cc][i];
     }
-    if (GATED) {
-      const int ng = 32 * (oo >> 4) + (oo & 15), nu = ng + 16;
-      const int64_t tg = sat16(mulshift((int64_t)sum[0] + (a.bias ? a.bias[ng] : 0), a.rq[2 * ng], a.rq[2 * ng + 1]));
-      const int64_t tu =
-          sat16(mulshift((int64_t)sum[NW - 1] + (a.bias ? a.bias[nu] : 0), a.rq[2 * nu], a.rq[2 * nu + 1]));
-      const int64_t sg = silu16(tg, a.silu_Mi, a.silu_Si, a.silu_sh, a.luts + kLutSig);
-      const int64_t f = sat16(rshr(tu * sg, a.aux_shift));
-      const int64_t off = (int64_t)r * a.Nout + oo;
-      if (a.g_out) a.g_out[off] = (int16_t)sg;
-      if (a.f_out) a.f_out[off] = (int16_t)f;
-      if (a.q_out) a.q_out[off] = (int8_t)sat8(mulshift(f, a.q_M, a.q_S));
-    } else if (a.nseg > 0) {
-      // multi-output linear (epilogue none): the channel's segment and its output
-      int sgi = 0;
-      while (sgi + 1 < a.nseg && oo >= a.seg_start[sgi + 1]) ++sgi;
-      const int ld = a.seg_start[sgi + 1] - a.seg_start[sgi], col = oo - a.seg_start[sgi];
-      const int64_t v = mulshift((int64_t)sum[0] + (a.bias ? a.bias[oo] : 0), a.rq[2 * oo], a.rq[2 * oo + 1]);
-      if (a.seg_i8[sgi])
-        reinterpret_cast<int8_t*>(a.seg_out[sgi])[(int64_t)r * ld + col] = (int8_t)sat8(v);
-      else
-        reinterpret_cast<int16_t*>(a.seg_out[sgi])[(int64_t)r * ld + col] = (int16_t)sat16(v);
-    } else {
-      store_out(a, r, oo, linear_epilogue(sum[0], r, oo, a));
-    }
+    gemv_finish<GATED>(a, r, oo, sum[0], sum[NW - 1]);
   }
+}
+
+template <int RB, bool GATED>
+static cudaError_t launch_gemv_t(const LinearArgs& a, cudaStream_t st) {
+  const int nout = GATED ? a.Nout : a.N;
+  const bool narrow_blocks = a.K >= 8192;
+  const int cpb = narrow_blocks ? 4 : 8;
+  const dim3 grid((nout + cpb - 1) / cpb, (a.R + RB - 1) / RB);
+  return narrow_blocks ? launch_k(k_gemv<RB, GATED, 4>, grid, dim3(256), 0, st, a)
+                       : launch_k(k_gemv<RB, GATED, 8>, grid, dim3(256), 0, st, a);
 }
 
 // ---- tiled dp4a GEMM: 64 rows x 64 channels per block, 4x4 outputs per thread -----------
@@ -223,11 +248,8 @@ cudaError_t launch_linear(const LinearArgs& a, int path, cudaStream_t st) {
   if (a.R <= 0 || a.N <= 0) return cudaSuccess;
   if (path == 0) path = a.R <= 16 ? 1 : 2;
   if (path == 1) {
-    const int nout = a.gated ? a.Nout : a.N;
-    const int rb = a.R == 1 ? 1 : 4;
-    const dim3 grid((nout + 7) / 8, (a.R + rb - 1) / rb);
-    auto kern = a.R == 1 ? (a.gated ? k_gemv<1, true> : k_gemv<1, false>) : (a.gated ? k_gemv<4, true> : k_gemv<4, false>);
-    const cudaError_t e = launch_k(kern, grid, dim3(256), 0, st, a);
+    const cudaError_t e = a.R == 1 ? (a.gated ? launch_gemv_t<1, true>(a, st) : launch_gemv_t<1, false>(a, st))
+                                   : (a.gated ? launch_gemv_t<4, true>(a, st) : launch_gemv_t<4, false>(a, st));
     if (e != cudaSuccess) return e;
   } else {
     dim3 grid((a.N + TB - 1) / TB, (a.R + TB - 1) / TB);
