@@ -141,11 +141,14 @@ __global__ void k_attention(const int8_t* q, const int8_t* kc, const int8_t* vc,
 // ---------------------------------------------------------------------------------------
 constexpr int kDecThreads = 256, kDecWarps = kDecThreads / 32;
 
-// KV tiles of 8 KB (D <= 64) or 16 KB (D >= 128) stream through a ring of kRing stages;
+// KV tiles of 8 KB (D <= 64) or 16 KB (D >= 128) stream through a ring of dec_ring(D) stages;
 // at D >= 128 a tile has kDecThreads / dec_tpk(D) keys and dec_tpk(D) threads share a key.
-// Three stages keep 3 CTAs per SM resident at head dim 128 (with four, shared memory held 2,
-// and at 8 waves of short slices per layer the per-CTA latency chains went unhidden).
-constexpr int kRing = 3;
+// At head dim 128 two stages of 16 KB measured best: shared memory then holds more CTAs per
+// SM, which overlap one another's phases (C4 decode attention 128.7 -> 111.9 us per layer
+// against three stages; C5 unchanged; four stages held only 2 CTAs per SM and lost).  Head
+// dims up to 64 keep three stages of 8 KB.
+constexpr int kRingMax = 3;
+__host__ __device__ constexpr int dec_ring(int D) { return D >= 128 ? 2 : 3; }
 __host__ __device__ constexpr int dec_tile_keys(int D) { return (D >= 128 ? 16384 : 8192) / D; }
 __host__ __device__ constexpr int dec_tpk(int D) { return D >= 128 ? kDecThreads / dec_tile_keys(D) : 1; }
 
@@ -173,7 +176,7 @@ static size_t dec_p_bytes(int RB, int D, int max_seq, int C) {
 
 static size_t dec_smem_bytes(int RB, int D, int max_seq, int C) {
   const size_t cap = (size_t)dec_slice_cap(max_seq, C);
-  return (size_t)kRing * dec_tile_keys(D) * D + (size_t)RB * D + (size_t)RB * cap * 4 + dec_p_bytes(RB, D, max_seq, C) +
+  return (size_t)dec_ring(D) * dec_tile_keys(D) * D + (size_t)RB * D + (size_t)RB * cap * 4 + dec_p_bytes(RB, D, max_seq, C) +
          (size_t)RB * D * 4 + (size_t)kDecWarps * RB * 4 + (size_t)2 * RB * 4 + 128;
 }
 
@@ -302,7 +305,8 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
   static_assert(TPK == 1 || TK * TPK == kDecThreads, "one key per TPK threads");
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ uint16_t s_expi[16], s_expf[256];
-  __shared__ __align__(8) uint64_t full_bar[kRing];
+  constexpr int kRing = dec_ring(D);
+  __shared__ __align__(8) uint64_t full_bar[kRingMax];
   __shared__ int s_abort;
   __shared__ int32_t s_gmax[RB];
   __shared__ uint32_t s_inv[RB];
