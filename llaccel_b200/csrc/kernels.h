@@ -111,6 +111,14 @@ struct LinearArgs {
   unsigned long long* amax_key;
   int amax_vocab;
   int amax_base;
+  // RMSNorm folded into a one-row GEMV (R == 1; nx non-null): A is not read; every block
+  // computes it from the i16 row nx [K] into shared memory, exactly as the RMSNorm + quant
+  // step would (numerics.h:60-71): inv = min(65535, n_C / max(isqrt48(sum x^2 + n_eps), 1)),
+  // A = sat8(mulshift(sat16(rshr(x * g * inv, n_sh)), n_Mq, n_Sq)).
+  const int16_t* nx;
+  const int16_t* ngamma;
+  int64_t n_eps, n_C, n_Mq;
+  int n_sh, n_Sq;
 };
 
 // Tensor-parallel requant: acc [R][N] i32 (the all-reduced partial sums of a row-split

@@ -11,6 +11,7 @@
 // path lives in gemm_tc.cu; these stay as the small-batch path and as its cross-check.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 
 #include "kernels.h"
@@ -92,25 +93,85 @@ __device__ __forceinline__ void gemv_finish(const LinearArgs& a, int r, int oo, 
   }
 }
 
-template <int RB, bool GATED, int CPB>
+// The folded RMSNorm + quant of a one-row GEMV: the row nx [K] i16 -> xs [K] i8 in shared
+// memory (every thread of the block takes part; ends with a block barrier).
+__device__ __forceinline__ void gemv_norm_prologue(const LinearArgs& a, int8_t* xs) {
+  __shared__ uint64_t nsum[8];
+  __shared__ uint32_t ninv;
+  const uint4* xr = reinterpret_cast<const uint4*>(a.nx);  // written by the previous kernel: coherent loads
+  const uint4* gr = reinterpret_cast<const uint4*>(a.ngamma);
+  const int chunks = a.K >> 3;
+  uint64_t ss = 0;
+  for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+    const uint4 v = xr[c];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int32_t lo = (int16_t)(w[e] & 0xFFFF), hi = (int16_t)(w[e] >> 16);
+      ss += (uint32_t)(lo * lo) + (uint64_t)(uint32_t)(hi * hi);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) nsum[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint64_t t = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += nsum[i];
+    const uint32_t r = isqrt48_fast(t + (uint64_t)a.n_eps);
+    const uint64_t inv = udiv_fast((uint64_t)a.n_C, r > 1 ? r : 1);
+    ninv = (uint32_t)(inv > 65535 ? 65535 : inv);
+  }
+  __syncthreads();
+  const int64_t inv = ninv;
+  for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+    const uint4 v = xr[c], g = __ldg(gr + c);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w}, gw[4] = {g.x, g.y, g.z, g.w};
+    uint32_t q[2] = {0u, 0u};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int32_t x = (int16_t)((w[e >> 1] >> (16 * (e & 1))) & 0xFFFF);
+      const int32_t gg = (int16_t)((gw[e >> 1] >> (16 * (e & 1))) & 0xFFFF);
+      const int64_t y = sat16(rshr((int64_t)(x * gg) * inv, a.n_sh));
+      const int64_t qq = sat8(mulshift(y, a.n_Mq, a.n_Sq));
+      q[e >> 2] |= (uint32_t)(uint8_t)qq << (8 * (e & 3));
+    }
+    reinterpret_cast<uint2*>(xs)[c] = make_uint2(q[0], q[1]);
+  }
+  __syncthreads();
+}
+
+// The block walks channel groups g = blockIdx.x, + gridDim.x, ... (one group per block unless
+// the grid is smaller: the folded-norm launch caps it at 4 blocks per SM so that each block
+// normalises the row once); the next group's first round of weights is requested while the
+// current group's sums are reduced and stored.
+template <int RB, bool GATED, int CPB, bool NORM = false>
 __global__ void __launch_bounds__(256) k_gemv(LinearArgs a) {
   pdl_trigger();
+  static_assert(!NORM || RB == 1, "the folded RMSNorm serves one row");
+  extern __shared__ __align__(16) int8_t xs_norm[];  // NORM: the normalised, quantized row [K]
   constexpr int NW = GATED ? 2 : 1;        // weight rows per output channel
   constexpr int U = GATED ? 2 : 4;         // 16-byte loads per row and round
   constexpr int LPC = 32 / CPB;            // lanes per channel
   constexpr int SLOTS = 8 * LPC;           // K slots of the block
+  constexpr int STEP = SLOTS * U;          // K chunks per round of the block
   __shared__ int32_t part[8][NW][CPB][RB];  // [warp][row kind][channel][row]
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = lane / LPC, sub = lane % LPC;
   const int slot = w * LPC + sub;
-  const int o0 = blockIdx.x * CPB, r0 = blockIdx.y * RB;
-  const int o = o0 + c;
+  const int r0 = blockIdx.y * RB;
   const int nout = GATED ? a.Nout : a.N;
+  const int ngroups = (nout + CPB - 1) / CPB;
   const int nk = a.K >> 4;
-  const bool live = o < nout;
-  const int wrow = GATED ? 32 * (o >> 4) + (o & 15) : o;  // gate row (the up row is 16 further)
-  const uint4* wr0 = reinterpret_cast<const uint4*>(a.W + (int64_t)(live ? wrow : 0) * a.K);
-  const uint4* wr1 = wr0 + (int64_t)16 * nk;
+  bool live = false;
+  const uint4 *wr0 = nullptr, *wr1 = nullptr;
+  auto set_group = [&](int g) {
+    const int o = g * CPB + c;
+    live = o < nout;
+    const int wrow = GATED ? 32 * (o >> 4) + (o & 15) : o;  // gate row (the up row is 16 further)
+    wr0 = reinterpret_cast<const uint4*>(a.W + (int64_t)(live ? wrow : 0) * a.K);
+    wr1 = wr0 + (int64_t)16 * nk;
+  };
   auto fetch = [&](int k0, uint4 (&wv)[NW][U]) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -121,10 +182,6 @@ __global__ void __launch_bounds__(256) k_gemv(LinearArgs a) {
     }
   };
   int32_t acc[NW][RB];
-#pragma unroll
-  for (int h = 0; h < NW; ++h)
-#pragma unroll
-    for (int i = 0; i < RB; ++i) acc[h][i] = 0;
   auto consume = [&](int k0, const uint4 (&wv)[NW][U]) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -134,50 +191,66 @@ __global__ void __launch_bounds__(256) k_gemv(LinearArgs a) {
       for (int i = 0; i < RB; ++i) {
         const int r = r0 + i;
         if (r < a.R) {
-          // written by the previous kernel: a coherent load
-          const uint4 xv = reinterpret_cast<const uint4*>(a.A + (int64_t)r * a.K)[k];
+          // written by the previous kernel: a coherent load (or the folded norm's row)
+          const uint4 xv = NORM ? reinterpret_cast<const uint4*>(xs_norm)[k]
+                                : reinterpret_cast<const uint4*>(a.A + (int64_t)r * a.K)[k];
 #pragma unroll
           for (int h = 0; h < NW; ++h) acc[h][i] = dot16(wv[h][u], xv, acc[h][i]);
         }
       }
     }
   };
-  constexpr int STEP = SLOTS * U;  // K chunks per round of the block
   uint4 b0[NW][U], b1[NW][U];
+  int g = blockIdx.x;
+  set_group(g);
   fetch(slot, b0);
   pdl_wait();  // the activation rows and the output buffers belong to earlier kernels
-  for (int k0 = slot; k0 < nk; k0 += 2 * STEP) {
-    fetch(k0 + STEP, b1);  // next round in flight while this one is consumed
-    consume(k0, b0);
-    if (k0 + STEP >= nk) break;
-    fetch(k0 + 2 * STEP, b0);
-    consume(k0 + STEP, b1);
-  }
-#pragma unroll
-  for (int h = 0; h < NW; ++h)
-#pragma unroll
-    for (int i = 0; i < RB; ++i)
-#pragma unroll
-      for (int x = 1; x < LPC; x <<= 1) acc[h][i] += __shfl_xor_sync(0xffffffffu, acc[h][i], x);
-  if (sub == 0) {
+  if (NORM) gemv_norm_prologue(a, xs_norm);
+  for (; g < ngroups; g += gridDim.x) {
 #pragma unroll
     for (int h = 0; h < NW; ++h)
 #pragma unroll
-      for (int i = 0; i < RB; ++i) part[w][h][c][i] = acc[h][i];
-  }
-  __syncthreads();
-  for (int t = threadIdx.x; t < CPB * RB; t += blockDim.x) {
-    const int cc = t / RB, i = t % RB;
-    const int oo = o0 + cc, r = r0 + i;
-    if (oo >= nout || r >= a.R) continue;
-    int32_t sum[NW];
-#pragma unroll
-    for (int h = 0; h < NW; ++h) {
-      sum[h] = 0;
-#pragma unroll
-      for (int ww = 0; ww < 8; ++ww) sum[h] += part[ww][h][cc][i];
+      for (int i = 0; i < RB; ++i) acc[h][i] = 0;
+    for (int k0 = slot; k0 < nk; k0 += 2 * STEP) {
+      fetch(k0 + STEP, b1);  // next round in flight while this one is consumed
+      consume(k0, b0);
+      if (k0 + STEP >= nk) break;
+      fetch(k0 + 2 * STEP, b0);
+      consume(k0 + STEP, b1);
     }
-    gemv_finish<GATED>(a, r, oo, sum[0], sum[NW - 1]);
+    const int o0 = g * CPB;
+    // the next group's first round streams while this group's sums are reduced and stored
+    if (g + (int)gridDim.x < ngroups) {
+      set_group(g + gridDim.x);
+      fetch(slot, b0);
+    }
+#pragma unroll
+    for (int h = 0; h < NW; ++h)
+#pragma unroll
+      for (int i = 0; i < RB; ++i)
+#pragma unroll
+        for (int x = 1; x < LPC; x <<= 1) acc[h][i] += __shfl_xor_sync(0xffffffffu, acc[h][i], x);
+    if (sub == 0) {
+#pragma unroll
+      for (int h = 0; h < NW; ++h)
+#pragma unroll
+        for (int i = 0; i < RB; ++i) part[w][h][c][i] = acc[h][i];
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < CPB * RB; t += blockDim.x) {
+      const int cc = t / RB, i = t % RB;
+      const int oo = o0 + cc, r = r0 + i;
+      if (oo >= nout || r >= a.R) continue;
+      int32_t sum[NW];
+#pragma unroll
+      for (int h = 0; h < NW; ++h) {
+        sum[h] = 0;
+#pragma unroll
+        for (int ww = 0; ww < 8; ++ww) sum[h] += part[ww][h][cc][i];
+      }
+      gemv_finish<GATED>(a, r, oo, sum[0], sum[NW - 1]);
+    }
+    __syncthreads();  // part is reused by the next group
   }
 }
 
@@ -187,6 +260,21 @@ static cudaError_t launch_gemv_t(const LinearArgs& a, cudaStream_t st) {
   const bool narrow_blocks = a.K >= 8192;
   const int cpb = narrow_blocks ? 4 : 8;
   const dim3 grid((nout + cpb - 1) / cpb, (a.R + RB - 1) / RB);
+  if constexpr (RB == 1) {
+    if (a.nx) {  // the folded RMSNorm: K bytes of shared memory for the row
+      if (a.K > 16384 || a.K % 16) return cudaErrorInvalidValue;
+      // at most 4 blocks per SM, each normalising the row once and walking several groups
+      static int sms[64] = {};
+      int dev = 0;
+      cudaGetDevice(&dev);
+      if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+      if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+      const dim3 g1(std::min<unsigned>(grid.x, 4u * (unsigned)(sms[dev] > 0 ? sms[dev] : 148)), 1);
+      return narrow_blocks ? launch_k(k_gemv<1, GATED, 4, true>, g1, dim3(256), (size_t)a.K, st, a)
+                           : launch_k(k_gemv<1, GATED, 8, true>, g1, dim3(256), (size_t)a.K, st, a);
+    }
+  }
+  if (a.nx) return cudaErrorInvalidValue;
   return narrow_blocks ? launch_k(k_gemv<RB, GATED, 4>, grid, dim3(256), 0, st, a)
                        : launch_k(k_gemv<RB, GATED, 8>, grid, dim3(256), 0, st, a);
 }

@@ -129,7 +129,8 @@ static std::vector<int> step_ins(const Step& x) {
     std::vector<int> made;
     for (const Step& p : x.parts) {
       for (int a : step_ins(p))
-        if (std::find(made.begin(), made.end(), a) == made.end()) v.push_back(a);
+        if (std::find(made.begin(), made.end(), a) == made.end() && std::find(v.begin(), v.end(), a) == v.end())
+          v.push_back(a);  // each activation once, however many constituents read it
       for (int a : step_outs(p)) made.push_back(a);
     }
     return v;
@@ -951,6 +952,26 @@ static void pick_tc_tiling(int R, int N, int K, int sms, int* nt, int* ksplit) {
   *ksplit = ks;
 }
 
+// An RMSNorm (with its fused quant) followed by the linear that reads its quantized row: the
+// pair the one-row GEMV runs as one kernel, the norm in its prologue.  Needs the quantized
+// row read by that linear alone and the i16 row by nobody.
+static bool norm_pair(const llx_model* m, size_t i) {
+  if (i + 1 >= m->steps.size()) return false;
+  const Step& n = m->steps[i];
+  const Step& g = m->steps[i + 1];
+  if (n.kind != SK::RmsNorm || n.heads != 1 || n.out2 < 0 || n.K % 16 || n.K > 16384) return false;
+  if (!(g.kind == SK::Linear || g.kind == SK::LinearGroup || g.kind == SK::Gated)) return false;
+  return g.in == n.out2 && g.K == n.K && m->act_uses[n.out2] == 1 && m->act_uses[n.out] == 0;
+}
+
+static int gemm_path_for(const llx_model* m, int R);
+
+// The pair is run as one kernel in this launch: one row (batch-1 decode), the CUDA-core GEMV
+// path, activations not kept for dumps.
+static bool norm_folds_into_next(const llx_session* s, size_t i, int R) {
+  return R == 1 && !s->keep && gemm_path_for(s->m, R) == 1 && norm_pair(s->m, i);
+}
+
 static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, int M);
 
 // One tensor-core GEMM over R rows of activation `in` (N x K weights at a.W).  Many output
@@ -1051,7 +1072,25 @@ static void launch_output_argmax(llx_session* s, const void* logits, int R) {
 static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, int M) {
   llx_model* m = s->m;
   cudaStream_t st = s->st;
+  // a plan step (not a constituent of a fused one): an RMSNorm the next GEMV runs in its
+  // prologue launches nothing; that GEMV gets the norm's parameters
+  const Step* steps0 = m->steps.data();
+  const bool top = &x >= steps0 && &x < steps0 + m->steps.size();
+  const size_t idx = top ? (size_t)(&x - steps0) : 0;
+  if (top && norm_folds_into_next(s, idx, R)) return 0;
+  const Step* fold = top && idx > 0 && norm_folds_into_next(s, idx - 1, R) ? &m->steps[idx - 1] : nullptr;
   auto P = [&](int a) { return a < 0 ? nullptr : bd.p[a]; };
+  // the folded RMSNorm's row and parameters for the GEMV prologue
+  auto apply_fold = [&](LinearArgs& a) {
+    if (!fold) return;
+    a.nx = (const int16_t*)P(fold->in);
+    a.ngamma = (const int16_t*)dptr(m, fold->gamma_off);
+    a.n_eps = fold->eps_t;
+    a.n_C = fold->C;
+    a.n_sh = fold->sh_post;
+    a.n_Mq = fold->Mq;
+    a.n_Sq = fold->Sq;
+  };
   // an output that no later step reads (and no dump keeps) is not stored
   auto Pused = [&](int a) { return (a < 0 || (!s->keep && m->act_uses[a] == 0)) ? nullptr : bd.p[a]; };
   {
@@ -1095,6 +1134,7 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
           // argmax-only launches skip the logits store: nothing reads them
           if (!s->store_logits) a.out = nullptr;
         }
+        apply_fold(a);
         if (path == 3)
           e = launch_gemm_tc(s, bd, x.in, a, false);
         else
@@ -1241,6 +1281,7 @@ static int enqueue_one(llx_session* s, const Binding& bd, const Step& x, int R, 
           }
         }
         // tensor cores, or (few rows) the GEMV, which fuses the group / pair the same way
+        apply_fold(a);
         e = path == 3 ? launch_gemm_tc(s, bd, x.in, a, x.kind == SK::Gated) : launch_linear(a, 1, st);
         break;
       }
@@ -1353,6 +1394,10 @@ static void plan_arena(llx_session* s) {
       if (x.kind != SK::Attention || x.rope_step < 0) continue;
       for (int a : step_ins(m->steps[x.rope_step])) last[a] = std::max(last[a], i);
     }
+    // a norm folded into the next GEMV's prologue is read by that GEMV: its input lives
+    // through it, so the GEMV's output never takes the row other blocks are still reading
+    for (int i = 0; i + 1 < ns; ++i)
+      if (norm_pair(m, (size_t)i)) last[m->steps[i].in] = std::max(last[m->steps[i].in], i + 1);
     for (size_t a = 0; a < na; ++a) last[a] = std::max(last[a], def[a]);
     for (int i = 0; i <= ns; ++i) {
       for (size_t a = 0; a < na; ++a)
