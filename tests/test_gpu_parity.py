@@ -107,10 +107,10 @@ def test_stress_graphs_run_chunk_matches_oracle(tmp_path, cfg):
     (352, 2048, "none", 96), (1024, 40000, "none", 0), (160, 8, "none", 0)])
 @pytest.mark.parametrize("R", [1, 5, 16, 40, 128, 300])
 def test_linear_paths_match_oracle(tmp_path, K, N, epi, chain, R):
-    """Every GEMM schedule (GEMV, tiled dp4a, tcgen05: the swapped-operand decode kernel for
-    R <= 128 (path 3), the row-tile kernel with and without cluster split-K (path 4, and
-    path 3 above 128 rows)) on full-range int8 operands against the oracle, for all four
-    epilogues and i8 outputs."""
+    """Every GEMM schedule (GEMV, with several channel groups per block from N = 4736 at one
+    row; tiled dp4a; tcgen05: the swapped-operand decode kernel for R <= 32 (path 3), the
+    row-tile kernel with and without cluster split-K (path 4, and path 3 above 32 rows)) on
+    full-range int8 operands against the oracle, for all four epilogues and i8 outputs."""
     d = qgraph_synth.build_linear(tmp_path / "lin", K=K, N=N, epi=epi, chain_i8=chain, seed=K + N + R)
     o = O.OracleModel(d)
     rng = np.random.default_rng(R)
