@@ -295,7 +295,7 @@ __device__ __forceinline__ void dec_transpose4(uint32_t x0, uint32_t x1, uint32_
 }
 
 template <int LPK, int RB>
-__global__ void __launch_bounds__(kDecThreads) k_attention_decode(
+__device__ __forceinline__ void attention_decode_body(
     const int8_t* q, const int8_t* kc, const int8_t* vc, int8_t* out,
     int H, int Hkv, int max_seq, const int* d_pos, int64_t Ms, int Ss, int64_t Mo, int So, int prob_bits,
     const uint16_t* __restrict__ luts, int32_t* err, int C, const AttnArgs rope) {
@@ -870,6 +870,36 @@ __global__ void __launch_bounds__(kDecThreads) k_attention_decode(
     }
 }
 
+// The kernel, in two register budgets.  Head dim 128 with the tensor-core passes (4+ heads
+// per CTA) is held to 64 registers, which its slice state fits without spilling: 4 CTAs of
+// two 16 KB ring stages then share an SM instead of 3 (shared memory allows 4 up to max_seq
+// ~1500 at 4 heads).  The others keep the compiler's own allocation (an explicit minimum of
+// one CTA per SM would loosen it).
+#define LLX_DEC_PARAMS                                                                                         \
+  const int8_t *q, const int8_t *kc, const int8_t *vc, int8_t *out, int H, int Hkv, int max_seq, const int *d_pos, \
+      int64_t Ms, int Ss, int64_t Mo, int So, int prob_bits, const uint16_t *__restrict__ luts, int32_t *err, int C, \
+      const AttnArgs rope
+#define LLX_DEC_ARGS q, kc, vc, out, H, Hkv, max_seq, d_pos, Ms, Ss, Mo, So, prob_bits, luts, err, C, rope
+template <int LPK, int RB>
+__global__ void __launch_bounds__(kDecThreads) k_attention_decode(LLX_DEC_PARAMS) {
+  attention_decode_body<LPK, RB>(LLX_DEC_ARGS);
+}
+template <int LPK, int RB>
+__global__ void __launch_bounds__(kDecThreads, 4) k_attention_decode_r64(LLX_DEC_PARAMS) {
+  attention_decode_body<LPK, RB>(LLX_DEC_ARGS);
+}
+#undef LLX_DEC_PARAMS
+#undef LLX_DEC_ARGS
+using DecKernel = void (*)(const int8_t*, const int8_t*, const int8_t*, int8_t*, int, int, int, const int*, int64_t,
+                           int, int64_t, int, int, const uint16_t*, int32_t*, int, const AttnArgs);
+template <int LPK, int RB>
+static DecKernel dec_kernel() {
+  if constexpr (LPK == 8 && RB >= 4)
+    return k_attention_decode_r64<LPK, RB>;
+  else
+    return k_attention_decode<LPK, RB>;
+}
+
 // Resident clusters per cluster size, measured with the occupancy API at model load
 // (outside any stream capture) for each decode geometry: key (LPK, RB, max_seq, C).
 static std::mutex g_occ_mu;
@@ -891,7 +921,7 @@ static cudaError_t measure_dec_occupancy(int max_seq) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int clusters = 0;
-    const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, k_attention_decode<LPK, RB>, &cfg);
+    const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, dec_kernel<LPK, RB>(), &cfg);
     if (e != cudaSuccess) return e;
     std::lock_guard<std::mutex> lock(g_occ_mu);
     g_occ[std::make_tuple(LPK, RB, max_seq, C)] = clusters;
@@ -902,7 +932,10 @@ static cudaError_t measure_dec_occupancy(int max_seq) {
 // Cluster size: the largest C in {8, 4, 2} whose B * Hkv * groups clusters are all resident
 // at once (one wave: the slowest slice bounds the launch).  When no split fits in one wave
 // but one CTA per unit does, C = 1: every max / sum / output exchange is then a CTA barrier
-// instead of a cluster round trip.  Otherwise 2, and the hardware schedules the waves.
+// instead of a cluster round trip.  Beyond one wave: C = 1 again once one CTA per unit needs
+// 3 or more waves (the last wave's tail then costs less than the cluster exchanges: C5 at
+// 256 sequences, 2048 units over 444 resident CTAs, 158.6 against 177.7 us per layer), else
+// 2 (C4 at 64 sequences, 1.7 waves: 107.3 against 115.5 us with C = 1).
 template <int LPK, int RB>
 static int dec_cluster_size(int units, int max_seq) {
   std::lock_guard<std::mutex> lock(g_occ_mu);
@@ -910,6 +943,8 @@ static int dec_cluster_size(int units, int max_seq) {
     auto it = g_occ.find(std::make_tuple(LPK, RB, max_seq, C));
     if (it != g_occ.end() && it->second >= units) return C;
   }
+  auto c1 = g_occ.find(std::make_tuple(LPK, RB, max_seq, 1));
+  if (c1 != g_occ.end() && c1->second > 0 && units >= 3 * c1->second) return 1;
   return 2;
 }
 
@@ -918,7 +953,7 @@ static cudaError_t launch_dec_rb(const AttnArgs& a, cudaStream_t st) {
   const int groups = (a.H / a.Hkv + RB - 1) / RB;
   const int C = dec_cluster_size<LPK, RB>(a.B * a.Hkv * groups, a.max_seq);
   const size_t smem = dec_smem_bytes(RB, LPK * 16, a.max_seq, C);
-  const cudaError_t e = launch_kc(k_attention_decode<LPK, RB>, dim3(a.B * C, a.Hkv, groups), dim3(kDecThreads), smem,
+  const cudaError_t e = launch_kc(dec_kernel<LPK, RB>(), dim3(a.B * C, a.Hkv, groups), dim3(kDecThreads), smem,
                                   st, dim3(C, 1, 1), a.q, a.kc, a.vc, a.out, a.H, a.Hkv, a.max_seq, a.d_pos, a.Ms, a.Ss,
                                   a.Mo, a.So, a.prob_bits, a.luts, a.err, C, a);
   return e != cudaSuccess ? e : cudaGetLastError();
@@ -935,8 +970,7 @@ static cudaError_t launch_dec_l(const AttnArgs& a, cudaStream_t st) {
 }
 template <int LPK>
 static cudaError_t prep_dec_l(size_t smem) {
-  for (auto f : {k_attention_decode<LPK, 1>, k_attention_decode<LPK, 2>, k_attention_decode<LPK, 4>,
-                 k_attention_decode<LPK, 8>}) {
+  for (DecKernel f : {dec_kernel<LPK, 1>(), dec_kernel<LPK, 2>(), dec_kernel<LPK, 4>(), dec_kernel<LPK, 8>()}) {
     const cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
