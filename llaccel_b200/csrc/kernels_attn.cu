@@ -168,10 +168,10 @@ __host__ __device__ constexpr bool dec_tc(int D, int RB) { return (D == 64 || D 
 __host__ __device__ constexpr int dec_prow(int max_seq, int C, int TK) {
   return ((max_seq + C - 1) / C + TK - 1) / TK * TK + 16;
 }
-// bytes of the probability region: normalised p as i16 [RB][cap], or the hi / lo u8 planes
+// bytes of the probability region: the hi / lo u8 planes of the tensor-core value pass (the
+// CUDA-core value pass keeps normalised p in the score array, one int32 slot per key)
 static size_t dec_p_bytes(int RB, int D, int max_seq, int C) {
-  const size_t cap = (size_t)dec_slice_cap(max_seq, C);
-  return dec_tc(D, RB) ? (size_t)2 * RB * dec_prow(max_seq, C, dec_tile_keys(D)) : (size_t)RB * cap * 2;
+  return dec_tc(D, RB) ? (size_t)2 * RB * dec_prow(max_seq, C, dec_tile_keys(D)) : 0;
 }
 
 static size_t dec_smem_bytes(int RB, int D, int max_seq, int C) {
@@ -317,15 +317,14 @@ __device__ __forceinline__ void attention_decode_body(
   const int cap = dec_slice_cap(max_seq, C);
   int8_t* ring = reinterpret_cast<int8_t*>(smem);                        // [kRing][TK][D]
   int8_t* q_s = ring + (size_t)kRing * TK * D;                           // [RB][D]
-  int32_t* sc = reinterpret_cast<int32_t*>(q_s + RB * D);                // [RB][cap] scores, then p
-  // normalised p: i16 [RB][cap], or (tensor-core value pass) hi / lo u8 planes [RB][prow]
+  // [RB][cap] scores, then p, then (CUDA-core value pass) normalised p, each key in its slot
+  int32_t* sc = reinterpret_cast<int32_t*>(q_s + RB * D);
+  // tensor-core value pass: normalised p as hi / lo u8 planes [RB][prow]
   constexpr bool TC = dec_tc(D, RB);
   const int prow = dec_prow(max_seq, C, TK);
-  int16_t* pn16 = reinterpret_cast<int16_t*>(sc + (size_t)RB * cap);
-  uint8_t* p_hi = reinterpret_cast<uint8_t*>(pn16);
+  uint8_t* p_hi = reinterpret_cast<uint8_t*>(sc + (size_t)RB * cap);
   uint8_t* p_lo = p_hi + (size_t)RB * prow;
-  int32_t* opart = reinterpret_cast<int32_t*>(reinterpret_cast<unsigned char*>(pn16) +
-                                              (TC ? (size_t)2 * RB * prow : (size_t)RB * cap * 2));  // [RB][D]
+  int32_t* opart = reinterpret_cast<int32_t*>(p_hi + (TC ? (size_t)2 * RB * prow : 0));  // [RB][D]
   int32_t* wred = opart + RB * D;                                        // [warps][RB]
   int32_t* xmax = wred + kDecWarps * RB;                                 // [RB] slice maxima (read by peers)
   uint32_t* xsum = reinterpret_cast<uint32_t*>(xmax + RB);               // [RB] slice sums (read by peers)
@@ -676,10 +675,10 @@ __device__ __forceinline__ void attention_decode_body(
       }
     }
   } else {
+    // in place: each thread rewrites only the slots it reads
     for (int j = 0; j < rep; ++j) {
       const uint32_t inv = s_inv[j];
-      const int32_t* sj = sc + j * cap;
-      int16_t* pj = pn16 + (size_t)j * cap;
+      int32_t* sj = sc + j * cap;
       for (int t = threadIdx.x; t < cap; t += kDecThreads) {
         uint32_t v = 0;
         if (t < nkeys && live) {
@@ -687,7 +686,7 @@ __device__ __forceinline__ void attention_decode_body(
           const uint32_t pn = (x >> pshift) + ((x >> (pshift - 1)) & 1u);
           v = pn < pmax ? pn : pmax;
         }
-        pj[t] = (int16_t)v;  // entries past the slice stay 0: they weight the stale pair row
+        sj[t] = (int32_t)v;  // entries past the slice are 0: they weight the stale pair row
       }
     }
   }
@@ -797,7 +796,7 @@ __device__ __forceinline__ void attention_decode_body(
         if (it >= items) break;
         const int ph = it / units, u = it % units;
         const int j = u / D4, c4 = (u % D4) * 4;
-        const int16_t* pj = pn16 + (size_t)j * cap + lt0;
+        const int32_t* pj = sc + (size_t)j * cap + lt0;  // normalised p (< 2^15) per key
         // key pairs l, l + 1 with a compile-time stride per phase count
         auto pairs = [&](auto ks) {
           constexpr int KSC = decltype(ks)::value;
@@ -805,7 +804,9 @@ __device__ __forceinline__ void attention_decode_body(
             // the row after the last key may be stale shared memory: its pn is 0
             const uint32_t va = *reinterpret_cast<const uint32_t*>(tile + (size_t)l * D + c4);
             const uint32_t vb = *reinterpret_cast<const uint32_t*>(tile + (size_t)(l + 1) * D + c4);
-            const int pp = *reinterpret_cast<const int*>(pj + l);
+            // pn of keys l, l + 1 as the two 16-bit halves (l even, cap even: 8-byte aligned)
+            const uint2 p2 = *reinterpret_cast<const uint2*>(pj + l);
+            const int pp = (int)__byte_perm(p2.x, p2.y, 0x5410);
             const uint32_t lo = __byte_perm(va, vb, 0x5140), hi = __byte_perm(va, vb, 0x7362);
             acc[x][0] = __dp2a_lo(pp, (int)lo, acc[x][0]);
             acc[x][1] = __dp2a_hi(pp, (int)lo, acc[x][1]);
