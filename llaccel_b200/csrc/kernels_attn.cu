@@ -168,16 +168,32 @@ __host__ __device__ constexpr bool dec_tc(int D, int RB) { return (D == 64 || D 
 __host__ __device__ constexpr int dec_prow(int max_seq, int C, int TK) {
   return ((max_seq + C - 1) / C + TK - 1) / TK * TK + 16;
 }
+// Head dim 128 with the tensor-core passes (the 64-register instantiation) packs its shared
+// memory: the hi / lo probability bytes of each head go into that head's own score slots
+// (16-key groups of 16 hi then 16 lo bytes: key t near byte 2t, so written after the chunk's
+// scores are read they only cover slots already consumed), and the value pass's output
+// partials reuse the ring once the last value tile is consumed.
+__host__ __device__ constexpr bool dec_packed(int D, int RB) { return D == 128 && RB >= 4; }
+// int32 slots per head of the score array: the slice capacity, or (packed) at least the
+// probability bytes of the slice's whole tiles
+__host__ __device__ constexpr int dec_sstride(int max_seq, int C, int D, int RB) {
+  return dec_packed(D, RB) && ((max_seq + C - 1) / C + dec_tile_keys(D) - 1) / dec_tile_keys(D) * dec_tile_keys(D) / 2 >
+                                  dec_slice_cap(max_seq, C)
+             ? (((max_seq + C - 1) / C + dec_tile_keys(D) - 1) / dec_tile_keys(D) * dec_tile_keys(D) / 2 + 1) & ~1
+             : dec_slice_cap(max_seq, C);
+}
+
 // bytes of the probability region: the hi / lo u8 planes of the tensor-core value pass (the
-// CUDA-core value pass keeps normalised p in the score array, one int32 slot per key)
+// CUDA-core value pass keeps normalised p in the score array, one int32 slot per key; the
+// packed layout keeps the planes there too)
 static size_t dec_p_bytes(int RB, int D, int max_seq, int C) {
-  return dec_tc(D, RB) ? (size_t)2 * RB * dec_prow(max_seq, C, dec_tile_keys(D)) : 0;
+  return dec_tc(D, RB) && !dec_packed(D, RB) ? (size_t)2 * RB * dec_prow(max_seq, C, dec_tile_keys(D)) : 0;
 }
 
 static size_t dec_smem_bytes(int RB, int D, int max_seq, int C) {
-  const size_t cap = (size_t)dec_slice_cap(max_seq, C);
-  return (size_t)dec_ring(D) * dec_tile_keys(D) * D + (size_t)RB * D + (size_t)RB * cap * 4 + dec_p_bytes(RB, D, max_seq, C) +
-         (size_t)RB * D * 4 + (size_t)kDecWarps * RB * 4 + (size_t)2 * RB * 4 + 128;
+  const size_t ss = (size_t)dec_sstride(max_seq, C, D, RB);
+  return (size_t)dec_ring(D) * dec_tile_keys(D) * D + (size_t)RB * D + (size_t)RB * ss * 4 + dec_p_bytes(RB, D, max_seq, C) +
+         (dec_packed(D, RB) ? 0 : (size_t)RB * D * 4) + (size_t)kDecWarps * RB * 4 + (size_t)2 * RB * 4 + 128;
 }
 
 static int dec_rb(int rep) {
@@ -315,17 +331,23 @@ __device__ __forceinline__ void attention_decode_body(
   const int hg0 = blockIdx.z * RB;
   const int rep = min(RB, rep_all - hg0);
   const int cap = dec_slice_cap(max_seq, C);
+  constexpr bool PACKED = dec_packed(D, RB);
+  const int ss = dec_sstride(max_seq, C, D, RB);  // int32 slots per head of the score array
   int8_t* ring = reinterpret_cast<int8_t*>(smem);                        // [kRing][TK][D]
   int8_t* q_s = ring + (size_t)kRing * TK * D;                           // [RB][D]
-  // [RB][cap] scores, then p, then (CUDA-core value pass) normalised p, each key in its slot
+  // [RB][ss] scores, then p, then normalised p: each key in its slot (CUDA-core value pass),
+  // or as hi / lo bytes over the head's slots (packed)
   int32_t* sc = reinterpret_cast<int32_t*>(q_s + RB * D);
-  // tensor-core value pass: normalised p as hi / lo u8 planes [RB][prow]
+  // tensor-core value pass, unpacked: normalised p as hi / lo u8 planes [RB][prow]
   constexpr bool TC = dec_tc(D, RB);
   const int prow = dec_prow(max_seq, C, TK);
-  uint8_t* p_hi = reinterpret_cast<uint8_t*>(sc + (size_t)RB * cap);
+  uint8_t* p_hi = reinterpret_cast<uint8_t*>(sc + (size_t)RB * ss);
   uint8_t* p_lo = p_hi + (size_t)RB * prow;
-  int32_t* opart = reinterpret_cast<int32_t*>(p_hi + (TC ? (size_t)2 * RB * prow : 0));  // [RB][D]
-  int32_t* wred = opart + RB * D;                                        // [warps][RB]
+  // [RB][D] value partials: in the ring once it is free (packed), else after the planes;
+  // the exchange scratch below is live while value tiles land, so it never sits in the ring
+  int32_t* tail = reinterpret_cast<int32_t*>(p_hi + (TC && !PACKED ? (size_t)2 * RB * prow : 0));
+  int32_t* opart = PACKED ? reinterpret_cast<int32_t*>(ring) : tail;
+  int32_t* wred = PACKED ? tail : tail + RB * D;                         // [warps][RB]
   int32_t* xmax = wred + kDecWarps * RB;                                 // [RB] slice maxima (read by peers)
   uint32_t* xsum = reinterpret_cast<uint32_t*>(xmax + RB);               // [RB] slice sums (read by peers)
   const uint32_t crank = dec_cluster_rank();
@@ -470,21 +492,21 @@ __device__ __forceinline__ void attention_decode_body(
         }
         if (r < nk) {
           if (h0 < rep) {
-            sc[h0 * cap + lt0 + r] = c[0];
+            sc[h0 * ss + lt0 + r] = c[0];
             mxa = max(mxa, c[0]);
           }
           if (h1 < rep) {
-            sc[h1 * cap + lt0 + r] = c[1];
+            sc[h1 * ss + lt0 + r] = c[1];
             mxb = max(mxb, c[1]);
           }
         }
         if (r + 8 < nk) {
           if (h0 < rep) {
-            sc[h0 * cap + lt0 + r + 8] = c[2];
+            sc[h0 * ss + lt0 + r + 8] = c[2];
             mxa = max(mxa, c[2]);
           }
           if (h1 < rep) {
-            sc[h1 * cap + lt0 + r + 8] = c[3];
+            sc[h1 * ss + lt0 + r + 8] = c[3];
             mxb = max(mxb, c[3]);
           }
         }
@@ -508,7 +530,7 @@ __device__ __forceinline__ void attention_decode_body(
         for (int r = 0; r < RB; ++r)
           if (r < rep) {
             mxl[r] = max(mxl[r], sv[r]);
-            sc[r * cap + lt0 + l] = sv[r];
+            sc[r * ss + lt0 + l] = sv[r];
           }
       }
     } else {
@@ -540,7 +562,7 @@ __device__ __forceinline__ void attention_decode_body(
         for (int r = 0; r < RB; ++r)
           if (r < rep) {
             mxl[r] = max(mxl[r], sv[r]);
-            sc[r * cap + lt0 + l] = sv[r];
+            sc[r * ss + lt0 + l] = sv[r];
           }
       }
     }
@@ -606,10 +628,10 @@ __device__ __forceinline__ void attention_decode_body(
 #pragma unroll
         for (int j = 0; j < RB; ++j) {
           if (j < rep) {
-            const uint32_t d = (uint32_t)(mx[j] - sc[j * cap + t]);
+            const uint32_t d = (uint32_t)(mx[j] - sc[j * ss + t]);
             const uint32_t pr = FAST ? gap_prob_hi(d, (uint32_t)Ms, rnd, zsh, s_expi, s_expf)
                                      : gap_prob(d, (uint32_t)Ms, Ss, s_expi, s_expf);
-            sc[j * cap + t] = (int32_t)pr;
+            sc[j * ss + t] = (int32_t)pr;
             sum[j] += pr;
           }
         }
@@ -653,7 +675,42 @@ __device__ __forceinline__ void attention_decode_body(
   // p <= sum, so p * inv <= 2^31: the product and its rounding shift stay in 32 bits
   const uint32_t pmax = (1u << prob_bits) - 1u;
   const int pshift = 31 - prob_bits;
-  if constexpr (TC) {
+  if constexpr (PACKED) {
+    // hi / lo bytes of pn over whole tiles (0 past the slice), in the head's own score slots:
+    // 16-key group G at bytes 32 G (hi) and 32 G + 16 (lo), key u of a group at 4 (u % 4) +
+    // u / 4 as below.  Chunks of 512 keys: every thread reads its keys of the chunk, and after
+    // the barrier writes bytes < 2 (chunk end), i.e. slots below chunk end / 2, which belong
+    // to this chunk or earlier ones and have been read; later chunks' slots are untouched.
+    const int nfill = ntile * TK;
+    for (int c0 = 0; c0 < nfill; c0 += 2 * kDecThreads) {
+      uint32_t v[RB][2];
+#pragma unroll
+      for (int j = 0; j < RB; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int t = c0 + threadIdx.x + e * kDecThreads;
+          v[j][e] = 0;
+          if (j < rep && t < nkeys && live) {
+            const uint32_t x = (uint32_t)sc[j * ss + t] * s_inv[j];
+            const uint32_t pn = (x >> pshift) + ((x >> (pshift - 1)) & 1u);
+            v[j][e] = pn < pmax ? pn : pmax;
+          }
+        }
+      __syncthreads();
+#pragma unroll
+      for (int j = 0; j < RB; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int t = c0 + threadIdx.x + e * kDecThreads;
+          if (j < rep && t < nfill) {
+            const int u = t & 15;
+            uint8_t* at = reinterpret_cast<uint8_t*>(sc + (size_t)j * ss) + 32 * (t >> 4) + 4 * (u & 3) + (u >> 2);
+            at[0] = (uint8_t)(v[j][e] >> 8);
+            at[16] = (uint8_t)(v[j][e] & 255u);
+          }
+        }
+    }
+  } else if constexpr (TC) {
     // hi / lo bytes of pn (pn < 2^15) for the value MMAs, over whole tiles (0 past the
     // slice).  Within each 16-key half the value pass's MMA k index 4 tig + e stands for key
     // 4 e + tig, so key u of a half is stored at 4 (u % 4) + u / 4: a thread's 4 keys are
@@ -661,7 +718,7 @@ __device__ __forceinline__ void attention_decode_body(
     const int nfill = ntile * TK;
     for (int j = 0; j < rep; ++j) {
       const uint32_t inv = s_inv[j];
-      const int32_t* sj = sc + j * cap;
+      const int32_t* sj = sc + j * ss;
       for (int t = threadIdx.x; t < nfill; t += kDecThreads) {
         uint32_t v = 0;
         if (t < nkeys && live) {
@@ -678,7 +735,7 @@ __device__ __forceinline__ void attention_decode_body(
     // in place: each thread rewrites only the slots it reads
     for (int j = 0; j < rep; ++j) {
       const uint32_t inv = s_inv[j];
-      int32_t* sj = sc + j * cap;
+      int32_t* sj = sc + j * ss;
       for (int t = threadIdx.x; t < cap; t += kDecThreads) {
         uint32_t v = 0;
         if (t < nkeys && live) {
@@ -703,7 +760,8 @@ __device__ __forceinline__ void attention_decode_body(
     constexpr int CW = D / 16, MBH = D / 32;
     const int kc = warp & 3, half = warp >> 2;
     const bool wide = prob_bits > 8;
-    for (int i = threadIdx.x; i < rep * D; i += kDecThreads) opart[i] = 0;
+    if constexpr (!PACKED)
+      for (int i = threadIdx.x; i < rep * D; i += kDecThreads) opart[i] = 0;
     int32_t ah[MBH][4], al[MBH][4];
 #pragma unroll
     for (int m = 0; m < MBH; ++m)
@@ -739,7 +797,16 @@ __device__ __forceinline__ void attention_decode_body(
           dec_transpose4(xb[0], xb[1], xb[2], xb[3], wb);
         }
         uint32_t bl0 = 0, bl1 = 0, bh0 = 0, bh1 = 0;
-        if (g < rep) {
+        if (PACKED && g < rep) {
+          // the chunk's two 16-key groups: hi, lo, hi, lo (16 bytes each)
+          const uint8_t* pg = reinterpret_cast<const uint8_t*>(sc + (size_t)g * ss) + 2 * (lt0 + kc * 32) + 4 * tig;
+          bl0 = *reinterpret_cast<const uint32_t*>(pg + 16);
+          bl1 = *reinterpret_cast<const uint32_t*>(pg + 48);
+          if (wide) {
+            bh0 = *reinterpret_cast<const uint32_t*>(pg);
+            bh1 = *reinterpret_cast<const uint32_t*>(pg + 32);
+          }
+        } else if (g < rep) {
           const int pb = g * prow + lt0 + kc * 32 + 4 * tig;
           bl0 = *reinterpret_cast<const uint32_t*>(p_lo + pb);
           bl1 = *reinterpret_cast<const uint32_t*>(p_lo + pb + 16);
@@ -756,6 +823,10 @@ __device__ __forceinline__ void attention_decode_body(
       }
       __syncthreads();  // stage consumed by every thread
       if (threadIdx.x == 0 && i + kRing < 2 * ntile) issue(i + kRing);
+    }
+    if constexpr (PACKED) {
+      // the ring is free: every value tile has been consumed and none is in flight
+      for (int i = threadIdx.x; i < rep * D; i += kDecThreads) opart[i] = 0;
     }
     __syncthreads();  // opart zeroed by every thread before any adds
 #pragma unroll
@@ -796,7 +867,7 @@ __device__ __forceinline__ void attention_decode_body(
         if (it >= items) break;
         const int ph = it / units, u = it % units;
         const int j = u / D4, c4 = (u % D4) * 4;
-        const int32_t* pj = sc + (size_t)j * cap + lt0;  // normalised p (< 2^15) per key
+        const int32_t* pj = sc + (size_t)j * ss + lt0;  // normalised p (< 2^15) per key
         // key pairs l, l + 1 with a compile-time stride per phase count
         auto pairs = [&](auto ks) {
           constexpr int KSC = decltype(ks)::value;
