@@ -175,24 +175,42 @@ __device__ __forceinline__ void epi_unit(const LinearArgs& a, const int32_t (&ac
 // Fused gate/up unit: 8 output channels ob.. of row r from gate columns cg.. and up columns cu..
 //   sg = silu16(requant16(acc_g)); f = sat16(rshr(requant16(acc_u) * sg, aux_shift));
 //   fq = sat8(mulshift(f, q_M, q_S))
-__device__ __forceinline__ void epi_gated_unit(const LinearArgs& a, const int32_t (&ag)[8], const int32_t (&au)[8],
-                                               int cg, int cu, int r, int ob, const int64_t* s_bias,
-                                               const uint32_t* s_M, const int* s_S, const uint16_t* s_sig) {
+// The column loop stays rolled: each SM runs this epilogue once per launch, so its cost is
+// the first fetch of its instructions, and one column's body is an eighth of the unrolled
+// code.  The inputs shift through registers (constant indices) and the outputs are packed by
+// shifting in from the top, so nothing is indexed dynamically.
+__device__ __forceinline__ void epi_gated_unit(const LinearArgs& a, int32_t (&ag)[8], int32_t (&au)[8], int cg,
+                                               int cu, int r, int ob, const int64_t* s_bias, const uint32_t* s_M,
+                                               const int* s_S, const uint16_t* s_sig) {
   const bool narrow = a.narrow != 0;
   const uint32_t Mi = (uint32_t)a.silu_Mi;
-  int32_t sg[8], f[8], fq[8];
-#pragma unroll
+  uint64_t g_lo = 0, g_hi = 0, f_lo = 0, f_hi = 0, q8 = 0;
+#pragma unroll 1
   for (int j = 0; j < 8; ++j) {
-    const int32_t tg = requant_sat(ag[j], s_bias[cg + j], s_M[cg + j], s_S[cg + j], narrow, -32768, 32767);
-    const int32_t tu = requant_sat(au[j], s_bias[cu + j], s_M[cu + j], s_S[cu + j], narrow, -32768, 32767);
-    sg[j] = silu_fast(tg, Mi, a.silu_Si, a.silu_sh, s_sig);
-    f[j] = sat16_32(rshr_small(tu * sg[j], a.aux_shift));
-    fq[j] = mulshift_clamp(f[j], (uint32_t)a.q_M, a.q_S, -128, 127);
+    const int32_t tg = requant_sat(ag[0], s_bias[cg + j], s_M[cg + j], s_S[cg + j], narrow, -32768, 32767);
+    const int32_t tu = requant_sat(au[0], s_bias[cu + j], s_M[cu + j], s_S[cu + j], narrow, -32768, 32767);
+#pragma unroll
+    for (int k = 0; k < 7; ++k) {
+      ag[k] = ag[k + 1];
+      au[k] = au[k + 1];
+    }
+    const int32_t sg = silu_fast(tg, Mi, a.silu_Si, a.silu_sh, s_sig);
+    const int32_t f = sat16_32(rshr_small(tu * sg, a.aux_shift));
+    const int32_t fq = mulshift_clamp(f, (uint32_t)a.q_M, a.q_S, -128, 127);
+    g_lo = (g_lo >> 16) | (g_hi << 48);
+    g_hi = (g_hi >> 16) | ((uint64_t)(uint16_t)sg << 48);
+    f_lo = (f_lo >> 16) | (f_hi << 48);
+    f_hi = (f_hi >> 16) | ((uint64_t)(uint16_t)f << 48);
+    q8 = (q8 >> 8) | ((uint64_t)(uint8_t)fq << 56);
   }
   const int64_t off = (int64_t)r * a.Nout + ob;
-  if (a.g_out) store_i16<8>(a.g_out + off, sg);
-  if (a.f_out) store_i16<8>(a.f_out + off, f);
-  if (a.q_out) store_i8<8>(a.q_out + off, fq);
+  if (a.g_out)
+    *reinterpret_cast<uint4*>(a.g_out + off) = make_uint4((uint32_t)g_lo, (uint32_t)(g_lo >> 32), (uint32_t)g_hi,
+                                                          (uint32_t)(g_hi >> 32));
+  if (a.f_out)
+    *reinterpret_cast<uint4*>(a.f_out + off) = make_uint4((uint32_t)f_lo, (uint32_t)(f_lo >> 32), (uint32_t)f_hi,
+                                                          (uint32_t)(f_hi >> 32));
+  if (a.q_out) *reinterpret_cast<uint2*>(a.q_out + off) = make_uint2((uint32_t)q8, (uint32_t)(q8 >> 32));
 }
 
 template <int NT, int S>
