@@ -440,8 +440,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 
 // ---------------------------------------------------------------------------------------
 // Persistent variant for GEMMs with many output tiles (prefill, the vocabulary projection):
-// one CTA per SM walks tiles t = blockIdx.x + j * gridDim.x (channel tiles fastest, so
-// consecutive CTAs share an activation row tile in L2).  The accumulator is double-buffered
+// one CTA per SM walks tiles t = blockIdx.x + j * gridDim.x: with more rows than channels
+// (prefill) channel tiles fastest, so consecutive CTAs share an activation row tile in L2;
+// otherwise (decode batches against wide weights) row tiles fastest, so the row tiles of one
+// weight tile run in the same wave and the weight tile crosses HBM once.  The accumulator is double-buffered
 // in TMEM (2 x NT columns): the MMA warp fills buffer j & 1 while the EW epilogue warps drain
 // the other, so the integer epilogue of tile j overlaps the main loop of tile j + 1.
 // Barriers: full/empty per ring stage (TMA <-> MMA), acc_full/acc_empty per buffer
@@ -471,6 +473,11 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
   const int tiles = ntn * ntm;
   const int nkb = (a.K + BK - 1) / BK;
   const int my_tiles = blockIdx.x < tiles ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const bool rows_fast = a.N > a.R;
+  auto tile_origin = [&](int t, int& n0, int& m0) {
+    n0 = (rows_fast ? t / ntm : t % ntn) * NT;
+    m0 = (rows_fast ? t % ntm : t / ntn) * BM;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -504,8 +511,8 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
       int it = 0;
       bool waited = false;
       for (int j = 0; j < my_tiles && !abort_flag; ++j) {
-        const int t = blockIdx.x + j * gridDim.x;
-        const int n0 = (t % ntn) * NT, m0 = (t / ntn) * BM;
+        int n0, m0;
+        tile_origin(blockIdx.x + j * gridDim.x, n0, m0);
         for (int kb = 0; kb < nkb; ++kb, ++it) {
           const int s = it % S;
           if (it >= S && !mbar_wait(&empty_bar[s], ((it / S) + 1) & 1, &abort_flag)) {
@@ -577,8 +584,8 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     int best_r = -1;
     for (int j = 0; j < my_tiles; ++j) {
       const int b = j & 1, u = j >> 1;
-      const int t = blockIdx.x + j * gridDim.x;
-      const int n0 = (t % ntn) * NT, m0 = (t / ntn) * BM;
+      int n0, m0;
+      tile_origin(blockIdx.x + j * gridDim.x, n0, m0);
       // this tile's requant parameters (the previous tile's epilogue is done with them)
       for (int i = threadIdx.x - 64; i < NT; i += kEpiThreads) {
         const int n = n0 + i;
