@@ -162,8 +162,10 @@ __global__ void __launch_bounds__(64) k_rmsnorm(const int16_t* x, const int16_t*
              y8 ? reinterpret_cast<uint2*>(y8 + (int64_t)row * K) : nullptr);
 }
 
-// Wide rows (K >= 2048, e.g. Llama-3-8B's 4096): one 256-thread block per row, CPT chunks per
-// thread, so a small batch still spreads its rows over many SMs.  Same arithmetic.
+// Wide rows (K >= 2048, e.g. Llama-3-8B's 4096), or few rows (at most two per SM, e.g. a
+// 128-sequence decode step): one 256-thread block per row, CPT chunks per thread, so a small
+// batch still spreads its rows over many SMs and each thread's elementwise chain is short.
+// Same arithmetic.
 template <int CPT>
 __global__ void __launch_bounds__(256) k_rmsnorm_wide(const int16_t* x, const int16_t* __restrict__ gamma,
                                                       int16_t* y, int8_t* y8, int K,
@@ -206,8 +208,11 @@ cudaError_t launch_rmsnorm(const int16_t* x, const int16_t* gamma, int16_t* y, i
   if (nrows <= 0) return cudaSuccess;
   const int fastq = (Sq >= 32 && Mq >= 0 && Mq < (int64_t)1 << 31) ? 1 : 0;
   const int chunks = K / 8;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
   cudaError_t e;
-  if (K >= 2048) {
+  if (K >= 2048 || nrows <= 2 * sms) {
     const int cpt = (chunks + 255) / 256;
     auto kern = cpt <= 1 ? k_rmsnorm_wide<1> : cpt <= 2 ? k_rmsnorm_wide<2> : cpt <= 4 ? k_rmsnorm_wide<4> : k_rmsnorm_wide<8>;
     if (cpt > 8) return cudaErrorInvalidValue;
